@@ -1,0 +1,429 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-attention hot path on B200 (one JSON line on rank 0).
+
+Headline workload (BASELINE cfg2): fp16 paged decode, batch 32, 32 query /
+8 KV heads, head_dim 128, page_size 16, every sequence at ctx 4096, seeded
+N(0,1) K/V/Q, block table a seeded permutation of a 32x256-page pool.
+metric = decode HBM GB/s = algorithmic bytes (Q + K + V + O, FlashAttnTile's
+``bytes_attention("decode")``) / device time.
+
+* ``value``: K timed launches with inputs resident in HBM (537 MB per step,
+  4x the 126 MB L2; L2 is also flushed between steps), CUDA events per step
+  on the launching stream, max over ranks.
+* ``e2e``: the same step through the public op ``torch.ops.flashattn_tile.paged_decode``
+  as a serving step calls it -- the per-step inputs (q, page table, seq_lens)
+  copied from pinned host memory, the default host-side validation, the output
+  copied back to pinned host memory -- with the KV cache resident on the GPU.
+* ``cpu_baseline``: the numpy restatement of the reference's fp32 path
+  (oracle/) on the same cfg2 inputs, timed on this host's cores.
+* ``secondary``: the other hot-path kernels measured the same way (quantised
+  decode cfg4, varlen prefill cfg3 when built).
+
+Multi-GPU (torchrun, one rank per GPU): decode shards by (sequence, KV head)
+with no communication; every rank owns a cfg2-sized shard (weak scaling) and
+``value`` is the bytes of all ranks over the slowest rank's time.
+
+``--impl reference`` times the reference arm instead: the oracle port of the
+reference's fp32 CPU path on rank 0 with all host threads, one bounded sample
+of cfg2 (8 of the 32 sequences) per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+CFG2 = dict(batch=32, heads=32, kv_heads=8, head_dim=128, page_size=16, ctx=4096)
+FLUSH_BYTES = 256 << 20  # > 126 MB L2
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at cfg2 from the
+# committed ncu capture (profiles/decode_sm100_cfg2.md); None until captured.
+NCU_TRAFFIC_BYTES = {"decode_cfg2": None}
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU through NVML."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int, period_s: float = 0.05):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # NVML missing: report no clocks rather than fail the bench
+            self._nvml = None
+        self.period = period_s
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(int(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)))
+                self.reasons |= int(n.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict | None:
+        if self._nvml is None or not self.samples:
+            return None
+        names = [v for k, v in self.REASONS.items() if self.reasons & k and v != "gpu_idle"]
+        return {"sm_mhz": int(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------- workloads
+def make_decode_cfg2(device, seed: int, dtype=torch.float16):
+    c = CFG2
+    gen = torch.Generator(device=device).manual_seed(seed)
+    pages_per_seq = c["ctx"] // c["page_size"]
+    pool = c["batch"] * pages_per_seq
+    shape = (pool, c["page_size"], c["kv_heads"], c["head_dim"])
+    k = torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dtype)
+    v = torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dtype)
+    q = torch.randn((c["batch"], c["heads"], c["head_dim"]), generator=gen, device=device).to(dtype)
+    table = torch.randperm(pool, generator=gen, device=device).view(c["batch"], pages_per_seq).to(torch.int32)
+    lens = torch.full((c["batch"],), c["ctx"], dtype=torch.int32, device=device)
+    return q, k, v, table, lens
+
+
+def decode_bytes(lens, heads, kv_heads, head_dim, page_size, elem=2, scale_bytes=0):
+    from flashattntile_b200.autotune import bytes_decode_paged
+
+    return bytes_decode_paged(lens, heads, kv_heads, head_dim, page_size, q_bytes=2, kv_bytes=elem,
+                              scale_bytes=scale_bytes)
+
+
+def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None) -> list[float]:
+    """Per-step device milliseconds of fn() (CUDA events on the current stream)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush.zero_()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+# --------------------------------------------------------------------------- CPU arms
+def cpu_decode_rate(q, k, v, table, lens, seqs: int, iters: int, threads: int) -> tuple[float, float, str]:
+    """Oracle (numpy port of the reference fp32 path) on the first `seqs` sequences."""
+    import numpy as np
+
+    from oracle import attention as oatt
+
+    qn = q[:seqs].cpu().numpy()
+    tn = table[:seqs].cpu().numpy()
+    ln = lens[:seqs].cpu().numpy()
+    used = np.unique(tn.reshape(-1))
+    # Only the pages the sample reads are copied to the host.
+    remap = np.full(int(k.shape[0]), -1, dtype=np.int64)
+    remap[used] = np.arange(used.size)
+    idx = torch.from_numpy(used).to(k.device)
+    kn = k.index_select(0, idx).cpu().numpy()
+    vn = v.index_select(0, idx).cpu().numpy()
+    tn = remap[tn].astype(np.int32)
+    nbytes = decode_bytes(ln.tolist(), q.shape[1], k.shape[2], k.shape[3], k.shape[1])
+    times = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        oatt.attention_paged(qn, kn, vn, tn, ln, int(k.shape[1]), dtype="f16", threads=threads)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    sample = f"cfg2 sequences 0..{seqs - 1} ({seqs} x ctx {int(ln[0])}), fp16 inputs upcast to fp32, min of {iters}"
+    return nbytes / best / 1e9, best, sample
+
+
+# --------------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import datetime
+
+    import flashattntile_b200  # noqa: F401
+    from flashattntile_b200 import _lib
+    from flashattntile_b200.kernels.decode import launch_decode
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    peaks = _peaks()
+    c = CFG2
+    q, k, v, table, lens = make_decode_cfg2(device, seed=1 + rank)
+    lens_list = [c["ctx"]] * c["batch"]
+    nbytes = decode_bytes(lens_list, c["heads"], c["kv_heads"], c["head_dim"], c["page_size"])
+    scale = c["head_dim"] ** -0.5
+    out = torch.empty_like(q)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def step():
+        launch_decode(q, k, v, table, lens, c["page_size"], scale, 1, out=out)
+
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        times = time_steps(step, args.steps, args.warmup, flush)
+    torch.cuda.synchronize()
+    total_ms = sum(times)
+    if dist is not None:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    ms_per_step = total_ms / args.steps
+    value = world * nbytes / (ms_per_step * 1e-3) / 1e9
+    kernel_ms = statistics.mean(times)
+    achieved = nbytes / (kernel_ms * 1e-3) / 1e9
+    dev_err = _lib.read_device_error(device)
+
+    # ---- e2e through the public op with host buffers ----
+    q_h = q.cpu().pin_memory()
+    t_h = table.cpu().pin_memory()
+    l_h = lens.cpu().pin_memory()
+    o_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_d, t_d, l_d = torch.empty_like(q), torch.empty_like(table), torch.empty_like(lens)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        t_d.copy_(t_h, non_blocking=True)
+        l_d.copy_(l_h, non_blocking=True)
+        o = torch.ops.flashattn_tile.paged_decode(q_d, k, v, t_d, l_d, c["page_size"], scale, 1)
+        o_h.copy_(o, non_blocking=True)
+
+    e2e_times = time_steps(e2e_step, max(10, args.steps // 2), args.warmup, flush)
+    e2e_ms = sum(e2e_times) / len(e2e_times)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = q.numel() * q.element_size() + table.numel() * 4 + lens.numel() * 4
+    d2h = q.numel() * q.element_size()
+    e2e_ok = torch.allclose(o_h.to(device).float(), out.float(), atol=0, rtol=0)
+
+    secondary = {}
+    if not args.no_secondary:
+        secondary = run_secondary(device, args, peaks)
+    if dist is not None:
+        dist.barrier()
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            threads = os.cpu_count() or 1
+            rate, best, sample = cpu_decode_rate(q, k, v, table, lens, c["batch"], 3, threads)
+            cpu = {"value": round(rate, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
+                   "seconds_per_call": round(best, 4)}
+        traffic = NCU_TRAFFIC_BYTES["decode_cfg2"]
+        line = {
+            "metric": "decode HBM GB/s (cfg2: fp16 paged decode B32 ctx4096 H32/8 D128 ps16)",
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic N(0,1), seeded per rank",
+            "config": {"workload": "cfg2 paged decode", "batch_per_gpu": c["batch"], "global_batch": c["batch"] * world,
+                       "ctx": c["ctx"], "heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
+                       "page_size": c["page_size"], "parallelism": f"shard (sequence, kv-head) x{world}, no comm",
+                       "l2": "inputs 537 MB > 126 MB L2, and 256 MB L2 flush between steps"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_source": peaks["source"] + " copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": traffic, "algorithmic_bytes": nbytes, "kernel_ms": round(kernel_ms, 5)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * nbytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "torch.ops.flashattn_tile.paged_decode, default validation, pinned host q/table/lens/out",
+                    "matches_device_path": bool(e2e_ok)},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "device_error_word": dev_err,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_secondary(device, args, peaks) -> dict:
+    """Quantised decode (cfg4) and, when built, varlen prefill (cfg3)."""
+    from flashattntile_b200 import quant
+    from flashattntile_b200.kernels.decode import launch_decode
+
+    res = {}
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    batch, heads, kvh, dim, ps = 128, 32, 8, 128, 32
+    ctx = torch.randint(1024, 16385, (batch,), generator=gen)
+    pages = [math.ceil(int(n) / ps) for n in ctx]
+    pool = sum(pages)
+    g2 = torch.Generator(device=device).manual_seed(3)
+    perm = torch.randperm(pool, generator=g2, device=device).to(torch.int32)
+    table = torch.zeros((batch, max(pages)), dtype=torch.int32, device=device)
+    off = 0
+    for b, n in enumerate(pages):
+        table[b, :n] = perm[off:off + n]
+        off += n
+    lens = ctx.to(torch.int32).to(device)
+    q = torch.randn((batch, heads, dim), generator=g2, device=device).half()
+    for mode in ("int8", "float8_e4m3fn"):
+        kq = torch.empty((pool, ps, kvh, dim), dtype=torch.int8 if mode == "int8" else torch.float8_e4m3fn,
+                         device=device)
+        vq = torch.empty_like(kq)
+        ks = torch.empty((pool, kvh), dtype=torch.float32, device=device)
+        vs = torch.empty_like(ks)
+        step_pages = 4096
+        for p0 in range(0, pool, step_pages):
+            p1 = min(pool, p0 + step_pages)
+            kf = torch.randn((p1 - p0, ps, kvh, dim), generator=g2, device=device)
+            vf = torch.randn((p1 - p0, ps, kvh, dim), generator=g2, device=device)
+            a, b_, sa, sb, _ = quant.quantize_kv_pages(kf, vf, mode=mode)
+            kq[p0:p1], vq[p0:p1], ks[p0:p1], vs[p0:p1] = a, b_, sa, sb
+        out = torch.empty_like(q)
+        nbytes = decode_bytes(ctx.tolist(), heads, kvh, dim, ps, elem=1, scale_bytes=4)
+
+        def step():
+            launch_decode(q, kq, vq, table, lens, ps, dim ** -0.5, 1, k_scale=ks, v_scale=vs, out=out)
+
+        times = time_steps(step, max(10, args.steps // 2), args.warmup, None)
+        ms = statistics.mean(times)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[f"cfg4_decode_{mode}"] = {"value": round(gbs, 1), "unit": "GB/s", "ms": round(ms, 4),
+                                      "algorithmic_bytes": nbytes, "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)}
+        del kq, vq, ks, vs
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_reference_arm(args, rank: int, world: int) -> None:
+    """Reference CPU path (oracle port of reference.py fp32) on rank 0 only."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import attention as oatt
+
+    c = CFG2
+    seqs = 8
+    gen = torch.Generator().manual_seed(1)
+    pages_per_seq = c["ctx"] // c["page_size"]
+    shape = (seqs * pages_per_seq, c["page_size"], c["kv_heads"], c["head_dim"])
+    k = torch.randn(shape, generator=gen).half().numpy()
+    v = torch.randn(shape, generator=gen).half().numpy()
+    q = torch.randn((seqs, c["heads"], c["head_dim"]), generator=gen).half().numpy()
+    table = torch.randperm(shape[0], generator=gen).view(seqs, pages_per_seq).to(torch.int32).numpy()
+    lens = np.full(seqs, c["ctx"], dtype=np.int32)
+    threads = os.cpu_count() or 1
+    nbytes = decode_bytes(lens.tolist(), c["heads"], c["kv_heads"], c["head_dim"], c["page_size"])
+    for _ in range(args.warmup):
+        oatt.attention_paged(q, k, v, table, lens, c["page_size"], dtype="f16", threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oatt.attention_paged(q, k, v, table, lens, c["page_size"], dtype="f16", threads=threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = nbytes / dt / 1e9
+    sample = f"cfg2 sequences 0..{seqs - 1} of 32 (ctx 4096), fp16 inputs upcast to fp32 per step"
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "decode HBM GB/s (cfg2: fp16 paged decode B32 ctx4096 H32/8 D128 ps16)",
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "cfg2 paged decode", "batch": c["batch"], "ctx": c["ctx"], "heads": c["heads"],
+                   "kv_heads": c["kv_heads"], "head_dim": c["head_dim"], "page_size": c["page_size"]},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

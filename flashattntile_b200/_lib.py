@@ -1,0 +1,163 @@
+"""ctypes binding of ``libflashattn_sm100.so`` (the C ABI in include/flashattn_tile_b200.h).
+
+The library is built in-tree by ``flashattntile_b200.csrc.build`` and loaded
+lazily on first use.  There is no fallback: if the library is missing or the
+tensors are not on a CUDA device, calls raise ``RuntimeError``.
+
+Status codes from the C ABI map to Python exceptions: invalid arguments ->
+``ValueError``, unsupported shapes -> ``NotImplementedError``, CUDA failures
+and too-small scratch buffers -> ``RuntimeError``; the message is the
+library's ``fat_last_error()``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libflashattn_sm100.so"
+
+FAT_OK = 0
+FAT_ERR_INVALID_ARGUMENT = 1
+FAT_ERR_UNSUPPORTED = 2
+FAT_ERR_CUDA = 3
+FAT_ERR_WORKSPACE = 4
+
+FAT_DEVERR_TIMEOUT = 1
+FAT_DEVERR_BAD_PAGE = 2
+
+DTYPE_CODE = {
+    torch.float16: 0,
+    torch.bfloat16: 1,
+    torch.float32: 2,
+    torch.int8: 3,
+}
+if hasattr(torch, "float8_e4m3fn"):
+    DTYPE_CODE[torch.float8_e4m3fn] = 4
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_vp = ctypes.c_void_p
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); every symbol the public header declares.
+SIGNATURES: dict[str, tuple] = {
+    "fat_version": (ctypes.c_char_p, []),
+    "fat_last_error": (ctypes.c_char_p, []),
+    "fat_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "fat_paged_decode": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,
+         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp],
+    ),
+    "fat_gather_paged": (
+        _i32,
+        [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp],
+    ),
+}
+
+_LOCK = threading.Lock()
+_LIB: ctypes.CDLL | None = None
+_ERROR: str | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once (thread-safe); raise RuntimeError if it is missing."""
+    global _LIB, _ERROR
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            if not LIB_PATH.exists():
+                _ERROR = (f"{LIB_PATH.name} is not built; run `python -m flashattntile_b200.csrc.build` "
+                          "(or __graft_entry__.build())")
+                raise RuntimeError(_ERROR)
+            lib = ctypes.CDLL(os.fspath(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = lib
+    return _LIB
+
+
+def available() -> bool:
+    try:
+        load()
+        return True
+    except (OSError, RuntimeError):
+        return False
+
+
+def unavailable_reason() -> str:
+    if available():
+        return ""
+    return _ERROR or "library failed to load"
+
+
+def check(status: int, what: str) -> None:
+    if status == FAT_OK:
+        return
+    msg = load().fat_last_error().decode(errors="replace") or what
+    if status == FAT_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    if status == FAT_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(f"{what} failed (status {status}): {msg}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+# ---------------------------------------------------------------------------
+# Scratch buffers: one zero-filled buffer per (device, stream), grown on demand.
+# The decode kernel leaves its tickets zeroed on success, so calls ordered on
+# one stream can share the buffer; a call that reported a device error resets it.
+# ---------------------------------------------------------------------------
+_WS: dict[tuple[int, int], torch.Tensor] = {}
+_ERR: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
+    buf = _ERR.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[key] = buf
+    return buf
+
+
+def reset_workspace(device: torch.device) -> None:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
+    if key in _WS:
+        _WS[key].zero_()
+    if key in _ERR:
+        _ERR[key].zero_()
+
+
+def read_device_error(device: torch.device) -> int:
+    """Synchronously read (and clear) the device error word of this stream."""
+    word = error_word(device)
+    value = int(word.item())
+    if value:
+        reset_workspace(device)
+    return value

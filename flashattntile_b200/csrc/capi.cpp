@@ -1,0 +1,96 @@
+// extern "C" entry points of libflashattn_sm100.so (declared in
+// include/flashattn_tile_b200.h).  Each one packs its plain arguments and
+// forwards to the internal launcher; no C++ types cross the boundary.
+#include "../../include/flashattn_tile_b200.h"
+
+#include "decode.h"
+#include "gather.h"
+#include "host_util.h"
+
+extern "C" {
+
+const char* fat_version(void) { return "flashattn_tile_b200 0.1.0 sm_100a"; }
+
+const char* fat_last_error(void) { return fat::last_error(); }
+
+size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int num_kv_heads, int head_dim) {
+  return fat::decode_workspace_bytes(device, batch, num_heads, num_kv_heads, head_dim);
+}
+
+int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
+                     const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                     int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                     const int32_t* seq_lens, const float* k_scale, const float* v_scale,
+                     int64_t scale_stride_page, void* out, int64_t out_stride_b, int64_t out_stride_h, int batch,
+                     int num_heads, int num_kv_heads, int head_dim, int page_size, int q_dtype, int kv_dtype,
+                     int out_dtype, float softmax_scale, int split_k_hint, void* workspace, size_t workspace_bytes,
+                     int32_t* error_word, void* stream) {
+  fat::set_last_error("");
+  if (split_k_hint < 1 || split_k_hint > 64)
+    return fat::invalid("paged_decode: split_k must be in [1, 64], got " + std::to_string(split_k_hint));
+  fat::DecodeArgs a;
+  a.q = q;
+  a.q_sb = q_stride_b;
+  a.q_sh = q_stride_h;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.kv_sp = kv_stride_page;
+  a.kv_ss = kv_stride_slot;
+  a.kv_sh = kv_stride_head;
+  a.num_pages = num_pages;
+  a.page_table = page_table;
+  a.pt_sb = page_table_stride;
+  a.max_pages = max_pages;
+  a.seq_lens = seq_lens;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.scale_sp = scale_stride_page;
+  a.out = out;
+  a.o_sb = out_stride_b;
+  a.o_sh = out_stride_h;
+  a.batch = batch;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.page_size = page_size;
+  a.q_dtype = q_dtype;
+  a.kv_dtype = kv_dtype;
+  a.out_dtype = out_dtype;
+  a.softmax_scale = softmax_scale;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  a.error_word = error_word;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return fat::launch_paged_decode(a);
+}
+
+int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_page_bytes, int64_t stride_slot_bytes,
+                     int64_t stride_head_bytes, int64_t num_pages, const int32_t* page_table,
+                     int64_t page_table_stride, int64_t max_pages, const int32_t* seq_lens, void* out_k, void* out_v,
+                     int64_t max_len, int batch, int num_kv_heads, int page_size, int64_t row_bytes,
+                     int32_t* error_word, void* stream) {
+  fat::set_last_error("");
+  fat::GatherArgs a;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.sp_bytes = stride_page_bytes;
+  a.ss_bytes = stride_slot_bytes;
+  a.sh_bytes = stride_head_bytes;
+  a.num_pages = num_pages;
+  a.page_table = page_table;
+  a.pt_sb = page_table_stride;
+  a.max_pages = max_pages;
+  a.seq_lens = seq_lens;
+  a.out_k = out_k;
+  a.out_v = out_v;
+  a.max_len = max_len;
+  a.batch = batch;
+  a.num_kv_heads = num_kv_heads;
+  a.page_size = page_size;
+  a.row_bytes = row_bytes;
+  a.error_word = error_word;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return fat::launch_gather_paged(a);
+}
+
+}  // extern "C"

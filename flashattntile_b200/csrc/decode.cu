@@ -1,0 +1,878 @@
+// Single-query paged decode for sm_100a.
+//
+// Replaces FlashAttnTile's decode family (flashattn_tile/kernels/decode.py:46-447:
+// plain, GQA-grouped, split-K + LSE reduce, and INT8/FP8 kernels) with one
+// persistent kernel:
+//
+// * Work is flattened into 64-token chunks of (sequence, KV head, head group)
+//   units and split evenly over one CTA per SM.  Every CTA derives the same
+//   split from seq_lens on the device (no host sync, no tuning): each CTA
+//   owns a contiguous range of chunks, so the split adapts to ragged batches.
+//   A unit split across CTAs is merged by a log-sum-exp combine done by the
+//   last CTA that finishes a piece of it (an atomic ticket per unit); the
+//   math is decode.py:12-14 / 341-352 in base 2.
+// * One producer warp walks the CTA's chunks, reads the page table and issues
+//   TMA tile loads of each page slice ([rows, head_dim] of one KV head, 128-byte
+//   swizzled) into a ring of shared-memory stages guarded by mbarriers.  Each K/V
+//   page is read from HBM once per GQA group, not once per query head.
+// * Four consumer warps take 16 tokens each per stage.  Scores and P.V run on
+//   the tensor cores (mma.sync m16n8k16, fp32 accumulate) with the group's
+//   query heads as the M rows; P enters the P.V product as a 16-bit head plus
+//   a 16-bit remainder in the otherwise unused rows 8-15, so the probabilities
+//   keep ~fp32 precision, as in the reference's fp32 p.v (decode.py:120).
+//   Online softmax state lives in registers; row maxima use quad shuffles.
+// * INT8 / e4m3 caches are dequantised in registers: codes are widened to the
+//   query's 16-bit type (exact) and the per-(page, KV head) scales are folded
+//   into the score (K) and into p (V), as in decode.py:408-439.
+//
+// Every mbarrier wait is bounded; on a timeout the kernel records
+// FAT_DEVERR_TIMEOUT, drains its own TMA copies and returns.
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "decode.h"
+#include "host_util.h"
+
+namespace fat {
+namespace dec {
+
+constexpr int kWarps = 4;                  // consumer warps
+constexpr int kThreads = (kWarps + 1) * 32;  // + one producer warp
+constexpr int kChunk = 16 * kWarps;        // tokens per pipeline stage
+constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
+constexpr int kStageBudget = 160 * 1024;   // shared memory for the stage ring
+
+enum : int { kFirst = 1, kLast = 2, kFull = 4, kDone = 8 };
+
+struct Meta {
+  int flags;
+  int b;
+  int unit_local;  // kv_head * head_groups + head_group
+  int chunk;       // chunk index inside the unit
+  int seq_len;
+  int chunks_b;    // chunks per unit of this sequence
+  long long unit_base;  // flattened index of the unit's first chunk
+  float kscale[kChunk / 8];
+  float vscale[kChunk / 8];
+};
+
+struct Params {
+  const void* q;
+  long long q_sb, q_sh;
+  void* out;
+  long long o_sb, o_sh;
+  const int* page_table;
+  long long pt_sb;
+  const int* seq_lens;
+  const float* k_scale;
+  const float* v_scale;
+  long long s_sp;  // scale stride per page (head stride 1)
+  int batch, num_heads, num_kv_heads, group, head_groups, page_size, num_pages, box_rows, max_pages;
+  float scale_log2;
+  int out_f32;
+  float* ws_o;   // [grid][2][kRows][D]
+  float* ws_ml;  // [grid][2][kRows][2]
+  int* ws_count; // [units]
+  int* err;
+};
+
+template <int D, int EB>
+struct Layout {
+  static constexpr int kRowBytes = D * EB;                         // one token row of one KV head
+  static constexpr int kBoxBytes = kRowBytes >= 128 ? 128 : kRowBytes;  // TMA box row
+  static constexpr int kCB = kRowBytes / kBoxBytes;                // column boxes per row
+  static constexpr int kTile = kChunk * kRowBytes;                 // K (or V) bytes per stage
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kStages = (kStageBudget / kStage) > 8 ? 8 : (kStageBudget / kStage);
+  static constexpr int kQBytes = kRows * D * 2;
+  static constexpr int kMergeFloats = kWarps * kRows * (D + 8) + 2 * kWarps * kRows;
+  static constexpr size_t kSmem = 1024 /*align slack*/ + size_t(kStages) * kStage + size_t(kStages) * kQBytes +
+                                  size_t(kStages) * sizeof(Meta) + size_t(kMergeFloats) * 4 +
+                                  size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16;
+
+  // Shared address of byte column `bc` (multiple of 16) of token row `row` of a tile.
+  static __device__ __forceinline__ uint32_t addr(uint32_t tile, int row, int bc) {
+    if constexpr (kBoxBytes == 128) {
+      return tile + uint32_t(bc >> 7) * uint32_t(kChunk * 128) + swz128(uint32_t(row), uint32_t((bc & 127) >> 4));
+    } else {
+      return tile + uint32_t(row * kBoxBytes + bc);
+    }
+  }
+};
+
+__device__ __forceinline__ long long owner_of(long long x, long long total, int nc) {
+  return ((x + 1) * nc - 1) / total;
+}
+
+__device__ __forceinline__ long long range_start(long long c, long long total, int nc) { return c * total / nc; }
+
+// Consumer-group barrier (128 threads) on an mbarrier so that every wait is bounded.
+__device__ __forceinline__ bool consumer_sync(uint32_t bar, int& phase, int* err, volatile int* abort) {
+  mbar_arrive(bar);
+  bool ok = mbar_wait_bounded(bar, uint32_t(phase), err, abort);
+  phase ^= 1;
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
+// 8-bit KV codes -> 16-bit MMA operands, exactly (every int8 and every finite
+// e4m3 value is representable in fp16 and in bf16).  widen4 turns the four
+// bytes of a word into the pairs (byte0, byte1) and (byte2, byte3).
+// ---------------------------------------------------------------------------
+template <typename T, int KVT>
+struct Widen;
+
+// int8 -> fp16: with u = x + 128, the fp16 bit pattern 0x6400 | u is 1024 + u,
+// so subtracting 1152 leaves x.
+template <>
+struct Widen<__half, FAT_DTYPE_I8> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& p01, uint32_t& p23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
+    const uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+    const uint32_t magic = 0x64806480u;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(p01) : "r"(a), "r"(magic));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(p23) : "r"(b), "r"(magic));
+  }
+};
+
+// int8 -> bf16: with u = x + 128, the fp32 bit pattern 0x4B000000 | u is
+// 2^23 + u; subtracting 2^23 + 128 leaves x, which bf16 holds exactly.
+template <>
+struct Widen<__nv_bfloat16, FAT_DTYPE_I8> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& p01, uint32_t& p23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.f;
+    const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.f;
+    const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.f;
+    const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.f;
+    p01 = pack2<__nv_bfloat16>(f0, f1);
+    p23 = pack2<__nv_bfloat16>(f2, f3);
+  }
+};
+
+// e4m3 -> fp16 with the hardware pair conversion.
+template <>
+struct Widen<__half, FAT_DTYPE_E4M3> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& p01, uint32_t& p23) {
+    const uint16_t lo = static_cast<uint16_t>(w & 0xffffu);
+    const uint16_t hi = static_cast<uint16_t>(w >> 16);
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(p01) : "h"(lo));
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(p23) : "h"(hi));
+  }
+};
+
+// e4m3 -> bf16: placing the code's exponent/mantissa bits (eeee mmm) at bf16
+// bits 10..4 gives 2^(e-127) * 1.mmm (or the matching subnormal); one exact
+// multiply by 2^120 rebiases it to 2^(e-7) * 1.mmm.
+template <>
+struct Widen<__nv_bfloat16, FAT_DTYPE_E4M3> {
+  static __device__ __forceinline__ uint32_t pair(uint32_t two) {
+    const uint32_t r = ((two & 0x00800080u) << 8) | ((two & 0x007F007Fu) << 4);
+    uint32_t out;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(out) : "r"(r), "r"(0x7B807B80u));
+    return out;
+  }
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& p01, uint32_t& p23) {
+    p01 = pair(__byte_perm(w, 0u, 0x4140));
+    p23 = pair(__byte_perm(w, 0u, 0x4342));
+  }
+};
+
+template <typename T, int D, int KVT>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                        const Params p) {
+  constexpr int EB = (KVT == FAT_DTYPE_I8 || KVT == FAT_DTYPE_E4M3) ? 1 : 2;
+  using L = Layout<D, EB>;
+  constexpr int kStages = L::kStages;
+  constexpr int NT = D / 8;  // n-tiles of the output
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  T* qarea = reinterpret_cast<T*>(smem + size_t(kStages) * L::kStage);
+  Meta* meta = reinterpret_cast<Meta*>(reinterpret_cast<uint8_t*>(qarea) + size_t(kStages) * L::kQBytes);
+  float* mO = reinterpret_cast<float*>(meta + kStages);
+  float* mM = mO + kWarps * kRows * (D + 8);
+  float* mL = mM + kWarps * kRows;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(mL + kWarps * kRows);
+  volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 1);  // [0] abort [1] last-flag
+  long long* shl = reinterpret_cast<long long*>(const_cast<int*>(shi) + 4);   // [0] start_b [1] start_S [2] total
+  long long* scan = shl + 4;                                                    // [kThreads]
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8u * kStages;
+  const uint32_t csync = full0 + 16u * kStages;
+  const int nkg = p.num_kv_heads * p.head_groups;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, kWarps);
+    }
+    mbar_init(csync, kWarps * 32);
+    shi[0] = 0;
+    shi[1] = 0;
+    shl[0] = -1;
+    fence_barrier_init();
+  }
+
+  // ---- every CTA derives the same balanced split of all chunks -------------
+  {
+    const int per = (p.batch + kThreads - 1) / kThreads;
+    const int b0 = tid * per;
+    const int b1 = min(p.batch, b0 + per);
+    long long mine = 0;
+    for (int b = b0; b < b1; ++b) mine += (max(__ldg(p.seq_lens + b), 0) + kChunk - 1) / kChunk;
+    scan[tid] = mine;
+    __syncthreads();
+    if (tid == 0) {
+      long long run = 0;
+      for (int t = 0; t < kThreads; ++t) {
+        long long v = scan[t];
+        scan[t] = run;
+        run += v;
+      }
+      shl[2] = run;
+    }
+    __syncthreads();
+    const long long total = shl[2] * nkg;
+    const long long x0 = range_start(blockIdx.x, total, gridDim.x);
+    const long long pre = scan[tid] * nkg;
+    if (x0 < total && pre <= x0 && x0 < pre + mine * nkg) {
+      long long s = scan[tid];
+      for (int b = b0; b < b1; ++b) {
+        const long long cb = (max(__ldg(p.seq_lens + b), 0) + kChunk - 1) / kChunk;
+        if (x0 < (s + cb) * nkg) {
+          shl[0] = b;
+          shl[1] = s;
+          break;
+        }
+        s += cb;
+      }
+    }
+    __syncthreads();
+  }
+  const long long total = shl[2] * nkg;
+  const long long x0 = range_start(blockIdx.x, total, gridDim.x);
+  const long long x1 = range_start(blockIdx.x + 1, total, gridDim.x);
+  volatile int* abort_flag = shi;
+
+  // Sequences without cached tokens own no chunks: their output rows are zero.
+  for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+    if (__ldg(p.seq_lens + b) > 0) continue;
+    for (int idx = tid; idx < p.num_heads * D; idx += kThreads) {
+      const int h = idx / D, d = idx - h * D;
+      const long long off = (long long)b * p.o_sb + (long long)h * p.o_sh + d;
+      if (p.out_f32) {
+        reinterpret_cast<float*>(p.out)[off] = 0.f;
+      } else {
+        reinterpret_cast<T*>(p.out)[off] = from_float<T>(0.f);
+      }
+    }
+  }
+
+  if (warp == kWarps) {
+    // ======================= producer warp =======================
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
+    int it = 0;
+    if (x0 < x1) {
+      int b = int(shl[0]);
+      long long S = shl[1];
+      int len = max(__ldg(p.seq_lens + b), 0);
+      int chunks_b = (len + kChunk - 1) / kChunk;
+      long long pos = x0 - S * nkg;
+      bool full_seg = false;
+      for (long long x = x0; x < x1; ++x) {
+        const int unit_local = int(pos / chunks_b);
+        const int chunk = int(pos - (long long)unit_local * chunks_b);
+        const bool first = (x == x0) || chunk == 0;
+        const bool last = (x == x1 - 1) || chunk == chunks_b - 1;
+        if (first) full_seg = (chunk == 0) && (x1 - x >= chunks_b);
+        const int s = it % kStages;
+        const uint32_t parity = uint32_t(((it / kStages) & 1) ^ 1);
+        if (!mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) break;
+
+        const int kvh = unit_local / p.head_groups;
+        const int hg = unit_local - kvh * p.head_groups;
+        const int tok0 = chunk * kChunk;
+        const int valid = min(kChunk, len - tok0);
+        const int nbox = (valid + p.box_rows - 1) / p.box_rows;
+        int phys = -1;
+        if (lane < nbox) {
+          const int t = tok0 + lane * p.box_rows;
+          const int lp = t / p.page_size;
+          phys = lp < p.max_pages ? __ldg(p.page_table + (long long)b * p.pt_sb + lp) : -1;
+          if (phys < 0 || phys >= p.num_pages) {
+            raise_error(p.err, FAT_DEVERR_BAD_PAGE);
+            phys = -1;
+          }
+        }
+        const unsigned okmask = __ballot_sync(0xffffffffu, phys >= 0);
+        Meta& mt = meta[s];
+        if constexpr (EB == 1) {
+          // One scale pair per 8-token group of the chunk; groups past the
+          // sequence end (or on a rejected page) get 0 so that masked tokens
+          // never meet stale shared memory.
+          float ksc = 0.f, vsc = 0.f;
+          if (phys >= 0) {
+            ksc = __ldg(p.k_scale + (long long)phys * p.s_sp + kvh);
+            vsc = __ldg(p.v_scale + (long long)phys * p.s_sp + kvh);
+          }
+          const int per8 = p.box_rows / 8;  // 8-token groups per box
+          const int src = (lane & 7) / per8;
+          const float kg = __shfl_sync(0xffffffffu, ksc, src);
+          const float vg = __shfl_sync(0xffffffffu, vsc, src);
+          if (lane < kChunk / 8) {
+            mt.kscale[lane] = kg;
+            mt.vscale[lane] = vg;
+          }
+        }
+        if (first) {
+          // Query rows of this head group -> qarea[s] (zero rows past the group).
+          const int rows = min(kRows, p.group - hg * kRows);
+          const int h0 = kvh * p.group + hg * kRows;
+          constexpr int kVec = D * 2 / 16;  // 16-byte vectors per row
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(qarea) + size_t(s) * L::kQBytes);
+          for (int i = lane; i < kRows * kVec; i += 32) {
+            const int r = i / kVec, v = i - r * kVec;
+            uint4 val = make_uint4(0, 0, 0, 0);
+            if (r < rows) {
+              const T* src = reinterpret_cast<const T*>(p.q) + (long long)b * p.q_sb + (long long)(h0 + r) * p.q_sh;
+              val = __ldg(reinterpret_cast<const uint4*>(src) + v);
+            }
+            dst[i] = val;
+          }
+        }
+        if (lane == 0) {
+          mt.flags = (first ? kFirst : 0) | (last ? kLast : 0) | (full_seg ? kFull : 0);
+          mt.b = b;
+          mt.unit_local = unit_local;
+          mt.chunk = chunk;
+          mt.seq_len = len;
+          mt.chunks_b = chunks_b;
+          mt.unit_base = S * nkg + (long long)unit_local * chunks_b;
+        }
+        __syncwarp();
+        const uint32_t bytes = uint32_t(__popc(okmask)) * uint32_t(p.box_rows) * uint32_t(L::kRowBytes) * 2u;
+        const uint32_t fb = full0 + 8u * s;
+        if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
+        __syncwarp();
+        const int nops = nbox * L::kCB * 2;
+        const uint32_t st = smem_u32(stages) + uint32_t(s) * L::kStage;
+        for (int j0 = 0; j0 < nops; j0 += 32) {
+          const int j = j0 + lane;
+          const int box = min(j, nops - 1) / (L::kCB * 2);
+          const int ph = __shfl_sync(0xffffffffu, phys, box);
+          if (j < nops && ph >= 0) {
+            const int rem = j - box * (L::kCB * 2);
+            const int tensor = rem / L::kCB;
+            const int cb = rem - tensor * L::kCB;
+            const int t = tok0 + box * p.box_rows;
+            const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(cb) * uint32_t(kChunk * L::kBoxBytes) +
+                                 uint32_t(box * p.box_rows * L::kBoxBytes);
+            tma_load_4d(dst, tensor ? &tm_v : &tm_k, fb, cb * (L::kBoxBytes / EB), kvh, t % p.page_size, ph);
+          }
+        }
+        ++it;
+        ++pos;
+        if (pos == (long long)chunks_b * nkg && x + 1 < x1) {
+          // advance to the next sequence with cached tokens
+          S += chunks_b;
+          pos = 0;
+          do {
+            ++b;
+            len = max(__ldg(p.seq_lens + b), 0);
+            chunks_b = (len + kChunk - 1) / kChunk;
+          } while (chunks_b == 0 && b + 1 < p.batch);
+        }
+      }
+    }
+    // Termination marker (or, after an abort, drain this CTA's own copies).
+    if (!*abort_flag) {
+      const int s = it % kStages;
+      const uint32_t parity = uint32_t(((it / kStages) & 1) ^ 1);
+      if (mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) {
+        if (lane == 0) {
+          meta[s].flags = kDone;
+          mbar_arrive(full0 + 8u * s);
+        }
+      }
+    }
+    if (*abort_flag && lane == 0) {
+      for (int k = max(0, it - kStages); k < it; ++k) {
+        mbar_wait_bounded(full0 + 8u * (k % kStages), uint32_t((k / kStages) & 1), nullptr, nullptr);
+      }
+    }
+    return;
+  }
+
+  // ======================= consumer warps =======================
+  const int g = lane >> 2;
+  const int c = lane & 3;
+  const int ctid = tid;  // 0..127
+  float o[NT][4];
+  float m_run = -CUDART_INF_F, l_run = 0.f;
+  uint32_t qa[D / 16][2];
+  int it = 0;
+  int cphase = 0;
+
+  while (true) {
+    const int s = it % kStages;
+    if (!mbar_wait_bounded(full0 + 8u * s, uint32_t((it / kStages) & 1), p.err, abort_flag)) break;
+    const Meta& mt = meta[s];
+    const int flags = mt.flags;
+    if (flags & kDone) break;
+    const int b = mt.b, unit_local = mt.unit_local, chunk = mt.chunk, seq_len = mt.seq_len, chunks_b = mt.chunks_b;
+    const long long unit_base = mt.unit_base;
+
+    if (flags & kFirst) {
+      m_run = -CUDART_INF_F;
+      l_run = 0.f;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      const T* qs = reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(qarea) + size_t(s) * L::kQBytes);
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        // 8-bit caches use a permuted reduction order (see the K fragments below).
+        const int d0 = (EB == 2) ? ks * 16 + 2 * c : c * (D / 4) + 4 * ks;
+        const int d1 = (EB == 2) ? ks * 16 + 8 + 2 * c : c * (D / 4) + 4 * ks + 2;
+        qa[ks][0] = *reinterpret_cast<const uint32_t*>(qs + g * D + d0);
+        qa[ks][1] = *reinterpret_cast<const uint32_t*>(qs + g * D + d1);
+      }
+    }
+
+    const int tok0 = chunk * kChunk + warp * 16;
+    const int nvalid = seq_len - tok0;
+    const uint32_t kt = smem_u32(stages) + uint32_t(s) * L::kStage;
+    const uint32_t vt = kt + L::kTile;
+    if (nvalid > 0) {
+      if (nvalid < 16) {
+        // Rows past the sequence may hold anything (even NaN): zero their V so
+        // that p = 0 contributes exactly nothing.
+        constexpr int kVecPerRow = L::kRowBytes / 16;
+        for (int i = lane; i < (16 - nvalid) * kVecPerRow; i += 32) {
+          const int r = nvalid + i / kVecPerRow;
+          const int bc = (i % kVecPerRow) * 16;
+          const uint32_t a = L::addr(vt, warp * 16 + r, bc);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+        }
+        __syncwarp();
+      }
+
+      // ---- S = Q K^T for 16 tokens (two n-tiles) ----
+      float sacc[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+      if constexpr (EB == 2) {
+        const int row = warp * 16 + ((lane >> 4) << 3) + (lane & 7);
+        const int khalf = ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(L::addr(kt, row, (ks * 16 + khalf) * 2), b0, b1, b2, b3);
+          const uint32_t a[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+          MmaOp<T>::run(sacc[0], a, b0, b1);
+          MmaOp<T>::run(sacc[1], a, b2, b3);
+        }
+      } else {
+        // 8-bit codes.  Lane (g, c) owns the reduction slice d in
+        // [c*D/4, (c+1)*D/4) of token rows g and g+8: k-step ks maps its k-slots
+        // (2c, 2c+1) to dims c*D/4 + 4ks + {0,1} and (2c+8, 2c+9) to + {2,3}.
+        // The same permutation was applied to the query fragments, so the dot
+        // products are unchanged; each lane reads contiguous bytes.
+        constexpr int kSlice = D / 4;  // bytes per lane per row
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int row = warp * 16 + j * 8 + g;
+#pragma unroll
+          for (int v = 0; v < kSlice / 16 + (kSlice % 16 ? 1 : 0); ++v) {
+            uint32_t wv[4];
+            const uint32_t a = L::addr(kt, row, c * kSlice + v * 16);
+            if constexpr (kSlice >= 16) {
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(wv[0]), "=r"(wv[1]), "=r"(wv[2]), "=r"(wv[3])
+                           : "r"(a));
+            } else {
+              asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(wv[0]), "=r"(wv[1]) : "r"(a));
+              wv[2] = wv[3] = 0u;
+            }
+#pragma unroll
+            for (int i = 0; i < (kSlice >= 16 ? 4 : 2); ++i) {
+              const int ks = v * 4 + i;
+              uint32_t b0, b1;
+              Widen<T, KVT>::run(wv[i], b0, b1);
+              const uint32_t av[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+              MmaOp<T>::run(sacc[j], av, b0, b1);
+            }
+          }
+        }
+      }
+
+      // ---- online softmax on the fragment (rows g: heads, cols: tokens) ----
+      const int toks[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
+      const float sv_raw[4] = {sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]};
+      float sv[4];
+      float ksc[2] = {1.f, 1.f}, vsc[2] = {1.f, 1.f};
+      if constexpr (EB == 1) {
+        const int grp = (warp * 16) / 8;
+        ksc[0] = mt.kscale[grp];
+        ksc[1] = mt.kscale[grp + 1];
+        vsc[0] = mt.vscale[grp];
+        vsc[1] = mt.vscale[grp + 1];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sv[i] = (toks[i] < nvalid) ? sv_raw[i] * (p.scale_log2 * ksc[i >> 1]) : -CUDART_INF_F;
+      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = fast_exp2(m_run - m_new);
+      float pr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pr[i] = fast_exp2(sv[i] - m_new);
+      l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+      m_run = m_new;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          o[n][0] *= alpha;
+          o[n][1] *= alpha;
+          o[n][2] *= alpha;
+          o[n][3] *= alpha;
+        }
+      }
+
+      // ---- O += P V : rows 0-7 carry P rounded to 16 bits, rows 8-15 the remainder ----
+      uint32_t pa[4];
+      split_hi_lo<T>(pr[0] * vsc[0], pr[1] * vsc[0], pa[0], pa[1]);
+      split_hi_lo<T>(pr[2] * vsc[1], pr[3] * vsc[1], pa[2], pa[3]);
+      if constexpr (EB == 2) {
+        const int row = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        const int dsel = (lane >> 4) << 3;
+#pragma unroll
+        for (int np = 0; np < D / 16; ++np) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(L::addr(vt, row, (np * 16 + dsel) * 2), b0, b1, b2, b3);
+          MmaOp<T>::run(o[2 * np], pa, b0, b1);
+          MmaOp<T>::run(o[2 * np + 1], pa, b2, b3);
+        }
+      } else {
+        // 8-bit V: lane (g, c) owns output dims [g*D/8, (g+1)*D/8) (B column g
+        // of n-tile nt is dim g*D/8 + nt) and reads token rows 2c, 2c+1, 2c+8,
+        // 2c+9; byte nt of two rows forms the pair of one B register.
+        constexpr int kSlice = D / 8;  // bytes per lane per row
+        const int rbase = warp * 16 + 2 * c;
+        uint32_t rw[4][kSlice / 4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int row = rbase + (r & 1) + (r >> 1) * 8;
+#pragma unroll
+          for (int v = 0; v < kSlice / 4; v += 4) {
+            const uint32_t a = L::addr(vt, row, g * kSlice + v * 4);
+            if constexpr (kSlice >= 16) {
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(rw[r][v]), "=r"(rw[r][v + 1]), "=r"(rw[r][v + 2]), "=r"(rw[r][v + 3])
+                           : "r"(a));
+            } else {
+              asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(rw[r][v]), "=r"(rw[r][v + 1]) : "r"(a));
+            }
+          }
+        }
+#pragma unroll
+        for (int w = 0; w < kSlice / 4; ++w) {
+          uint32_t b0a, b0b, b0c, b0d, b1a, b1b, b1c, b1d;
+          Widen<T, KVT>::run(__byte_perm(rw[0][w], rw[1][w], 0x5140), b0a, b0b);
+          Widen<T, KVT>::run(__byte_perm(rw[0][w], rw[1][w], 0x7362), b0c, b0d);
+          Widen<T, KVT>::run(__byte_perm(rw[2][w], rw[3][w], 0x5140), b1a, b1b);
+          Widen<T, KVT>::run(__byte_perm(rw[2][w], rw[3][w], 0x7362), b1c, b1d);
+          MmaOp<T>::run(o[4 * w + 0], pa, b0a, b1a);
+          MmaOp<T>::run(o[4 * w + 1], pa, b0b, b1b);
+          MmaOp<T>::run(o[4 * w + 2], pa, b0c, b1c);
+          MmaOp<T>::run(o[4 * w + 3], pa, b0d, b1d);
+        }
+      }
+      if (nvalid < 16) fence_proxy_async_smem();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8u * s);
+    ++it;
+
+    if (flags & kLast) {
+      // ---- end of this CTA's piece of a unit: merge the 4 warps ----
+      const float l_row = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
+      const float l_tot = l_row + __shfl_xor_sync(0xffffffffu, l_row, 2);
+      float* myO = mO + (warp * kRows + g) * (D + 8);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        if constexpr (EB == 2) {
+          *reinterpret_cast<float2*>(myO + n * 8 + 2 * c) = make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
+        } else {
+          myO[(2 * c) * (D / 8) + n] = o[n][0] + o[n][2];
+          myO[(2 * c + 1) * (D / 8) + n] = o[n][1] + o[n][3];
+        }
+      }
+      if (c == 0) {
+        mM[warp * kRows + g] = m_run;
+        mL[warp * kRows + g] = l_tot;
+      }
+      if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
+
+      const int kvh = unit_local / p.head_groups;
+      const int hg = unit_local - kvh * p.head_groups;
+      const int rows = min(kRows, p.group - hg * kRows);
+      const int h0 = kvh * p.group + hg * kRows;
+      const bool full = (flags & kFull) != 0;
+      const int slot = (x0 < unit_base) ? 1 : 0;
+      for (int idx = ctid; idx < rows * D; idx += kWarps * 32) {
+        const int gg = idx / D, d = idx - gg * D;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mM[w * kRows + gg]);
+        float Lsum = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+          const float wt = fast_exp2(mM[w * kRows + gg] - M);
+          Lsum += mL[w * kRows + gg] * wt;
+          O += mO[(w * kRows + gg) * (D + 8) + d] * wt;
+        }
+        if (full) {
+          const long long off = (long long)b * p.o_sb + (long long)(h0 + gg) * p.o_sh + d;
+          const float val = O / Lsum;
+          if (p.out_f32) {
+            reinterpret_cast<float*>(p.out)[off] = val;
+          } else {
+            reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
+          }
+        } else {
+          const long long base = ((long long)blockIdx.x * 2 + slot) * kRows + gg;
+          p.ws_o[base * D + d] = O;
+          if (d == 0) {
+            p.ws_ml[base * 2] = M;
+            p.ws_ml[base * 2 + 1] = Lsum;
+          }
+        }
+      }
+      if (!full) {
+        __threadfence();
+        if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
+        const long long unit = (long long)b * nkg + unit_local;
+        const int ca = int(owner_of(unit_base, total, gridDim.x));
+        const int cb = int(owner_of(unit_base + chunks_b - 1, total, gridDim.x));
+        if (ctid == 0) {
+          const int ticket = atomicAdd(p.ws_count + unit, 1);
+          shi[1] = (ticket == cb - ca) ? 1 : 0;
+        }
+        if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
+        if (shi[1]) {
+          __threadfence();
+          for (int idx = ctid; idx < rows * D; idx += kWarps * 32) {
+            const int gg = idx / D, d = idx - gg * D;
+            float M = -CUDART_INF_F;
+            for (int cc = ca; cc <= cb; ++cc) {
+              const int sl = (range_start(cc, total, gridDim.x) < unit_base) ? 1 : 0;
+              M = fmaxf(M, __ldcg(p.ws_ml + (((long long)cc * 2 + sl) * kRows + gg) * 2));
+            }
+            float Lsum = 0.f, O = 0.f;
+            for (int cc = ca; cc <= cb; ++cc) {
+              const int sl = (range_start(cc, total, gridDim.x) < unit_base) ? 1 : 0;
+              const long long base = ((long long)cc * 2 + sl) * kRows + gg;
+              const float wt = fast_exp2(__ldcg(p.ws_ml + base * 2) - M);
+              Lsum += __ldcg(p.ws_ml + base * 2 + 1) * wt;
+              O += __ldcg(p.ws_o + base * D + d) * wt;
+            }
+            const long long off = (long long)b * p.o_sb + (long long)(h0 + gg) * p.o_sh + d;
+            const float val = O / Lsum;
+            if (p.out_f32) {
+              reinterpret_cast<float*>(p.out)[off] = val;
+            } else {
+              reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
+            }
+          }
+          if (ctid == 0) p.ws_count[unit] = 0;  // leave the ticket zeroed for the next call
+        }
+      }
+      if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
+    }
+  }
+}
+
+}  // namespace dec
+}  // namespace fat
+
+// =============================================================================
+// Host side
+// =============================================================================
+namespace fat {
+namespace {
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  size_t o_off, ml_off, count_off, total;
+};
+
+WsLayout ws_layout(int grid, long long units, int head_dim) {
+  WsLayout w;
+  w.o_off = 0;
+  w.ml_off = align_up(size_t(grid) * 2 * dec::kRows * head_dim * sizeof(float), 256);
+  w.count_off = align_up(w.ml_off + size_t(grid) * 2 * dec::kRows * 2 * sizeof(float), 256);
+  w.total = align_up(w.count_off + size_t(units) * sizeof(int), 256);
+  return w;
+}
+
+template <typename T, int D, int KVT>
+int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
+  constexpr int EB = (KVT == FAT_DTYPE_I8 || KVT == FAT_DTYPE_E4M3) ? 1 : 2;
+  using L = dec::Layout<D, EB>;
+  auto kern = dec::paged_decode_kernel<T, D, KVT>;
+  static_assert(L::kSmem <= 227 * 1024, "decode stage ring exceeds shared memory");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kSmem));
+  if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(decode)", e);
+
+  const int box_rows = a.page_size < 16 ? a.page_size : 16;
+  const uint64_t dims[4] = {uint64_t(a.head_dim), uint64_t(a.num_kv_heads), uint64_t(a.page_size),
+                            uint64_t(a.num_pages)};
+  const uint64_t strides[3] = {uint64_t(a.kv_sh) * EB, uint64_t(a.kv_ss) * EB, uint64_t(a.kv_sp) * EB};
+  const uint32_t box[4] = {uint32_t(L::kBoxBytes / EB), 1u, uint32_t(box_rows), 1u};
+  const CUtensorMapDataType dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = L::kBoxBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUtensorMap tmk, tmv;
+  std::string why;
+  if (!encode_tiled(&tmk, dt, 4, a.k_cache, dims, strides, box, sw, &why)) return invalid("k_cache: " + why);
+  if (!encode_tiled(&tmv, dt, 4, a.v_cache, dims, strides, box, sw, &why)) return invalid("v_cache: " + why);
+
+  dec::Params p;
+  p.q = a.q;
+  p.q_sb = a.q_sb;
+  p.q_sh = a.q_sh;
+  p.out = a.out;
+  p.o_sb = a.o_sb;
+  p.o_sh = a.o_sh;
+  p.page_table = a.page_table;
+  p.pt_sb = a.pt_sb;
+  p.max_pages = int(a.max_pages);
+  p.seq_lens = a.seq_lens;
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
+  p.s_sp = a.scale_sp;
+  p.batch = a.batch;
+  p.num_heads = a.num_heads;
+  p.num_kv_heads = a.num_kv_heads;
+  p.group = a.num_heads / a.num_kv_heads;
+  p.head_groups = (p.group + dec::kRows - 1) / dec::kRows;
+  p.page_size = a.page_size;
+  p.num_pages = int(a.num_pages);
+  p.box_rows = box_rows;
+  p.scale_log2 = float(double(a.softmax_scale) * 1.4426950408889634);
+  p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
+  uint8_t* wsb = static_cast<uint8_t*>(a.workspace);
+  p.ws_o = reinterpret_cast<float*>(wsb + ws.o_off);
+  p.ws_ml = reinterpret_cast<float*>(wsb + ws.ml_off);
+  p.ws_count = reinterpret_cast<int*>(wsb + ws.count_off);
+  p.err = a.error_word;
+  (void)device;
+  kern<<<grid, dec::kThreads, L::kSmem, a.stream>>>(tmk, tmv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_failure("paged_decode launch", e);
+  return FAT_OK;
+}
+
+template <typename T, int KVT>
+int dispatch_dim(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
+  switch (a.head_dim) {
+    case 64:
+      return launch_t<T, 64, KVT>(a, device, grid, ws);
+    case 128:
+      return launch_t<T, 128, KVT>(a, device, grid, ws);
+    case 256:
+      return launch_t<T, 256, KVT>(a, device, grid, ws);
+    default:
+      return unsupported("paged_decode: head_dim must be 64, 128 or 256, got " + std::to_string(a.head_dim));
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+size_t decode_workspace_bytes(int device, int batch, int num_heads, int num_kv_heads, int head_dim) {
+  if (num_kv_heads <= 0 || num_heads <= 0 || batch < 0 || head_dim <= 0) return 0;
+  const int group = num_heads / num_kv_heads;
+  const long long units = (long long)batch * num_kv_heads * ((group + dec::kRows - 1) / dec::kRows);
+  return ws_layout(sm_count(device), units, head_dim).total;
+}
+
+int launch_paged_decode(const DecodeArgs& a) {
+  if (a.batch < 0) return invalid("paged_decode: batch must be non-negative");
+  if (a.num_heads <= 0 || a.num_kv_heads <= 0) return invalid("paged_decode: head counts must be positive");
+  if (a.num_heads % a.num_kv_heads != 0)
+    return invalid("paged_decode: num_heads " + std::to_string(a.num_heads) + " must be divisible by num_kv_heads " +
+                   std::to_string(a.num_kv_heads));
+  // Pages are moved in boxes of min(page_size, 16) token rows that must not
+  // straddle two pages: 8, or a multiple of 16 up to the TMA box limit.
+  if (!(a.page_size == 8 || (a.page_size % 16 == 0 && a.page_size <= 256)))
+    return unsupported("paged_decode: page_size must be 8 or a multiple of 16 up to 256, got " +
+                       std::to_string(a.page_size));
+  if (a.q_dtype != FAT_DTYPE_F16 && a.q_dtype != FAT_DTYPE_BF16)
+    return unsupported("paged_decode: q must be fp16 or bf16");
+  const bool quant = a.kv_dtype == FAT_DTYPE_I8 || a.kv_dtype == FAT_DTYPE_E4M3;
+  if (!quant && a.kv_dtype != a.q_dtype) return invalid("paged_decode: q dtype must match the cache dtype");
+  if (quant && (a.k_scale == nullptr || a.v_scale == nullptr))
+    return invalid("paged_decode: an int8/fp8 cache needs k_scale and v_scale");
+  if (a.out_dtype != a.q_dtype && a.out_dtype != FAT_DTYPE_F32)
+    return invalid("paged_decode: out dtype must be q's dtype or fp32");
+  if (a.batch == 0) return FAT_OK;
+  if (a.q == nullptr || a.k_cache == nullptr || a.v_cache == nullptr || a.page_table == nullptr ||
+      a.seq_lens == nullptr || a.out == nullptr || a.workspace == nullptr)
+    return invalid("paged_decode: null pointer argument");
+  if (a.num_pages <= 0 || a.max_pages <= 0) return invalid("paged_decode: empty cache or page table");
+  const int eb = quant ? 1 : 2;
+  if (!aligned16(a.k_cache) || !aligned16(a.v_cache) || (a.kv_sp * eb) % 16 || (a.kv_ss * eb) % 16 ||
+      (a.kv_sh * eb) % 16)
+    return unsupported("paged_decode: K/V base addresses and page/slot/head strides must be 16-byte aligned");
+  if (!aligned16(a.q) || (a.q_sb * 2) % 16 || (a.q_sh * 2) % 16)
+    return unsupported("paged_decode: q must be 16-byte aligned with 16-byte-multiple strides");
+
+  const int device = current_device();
+  const int grid = sm_count(device);
+  const int group = a.num_heads / a.num_kv_heads;
+  const long long units = (long long)a.batch * a.num_kv_heads * ((group + dec::kRows - 1) / dec::kRows);
+  const WsLayout ws = ws_layout(grid, units, a.head_dim);
+  if (a.workspace_bytes < ws.total)
+  {
+    set_last_error("paged_decode: workspace holds " + std::to_string(a.workspace_bytes) + " bytes, needs " +
+                   std::to_string(ws.total));
+    return FAT_ERR_WORKSPACE;
+  }
+
+  if (a.q_dtype == FAT_DTYPE_F16) {
+    switch (a.kv_dtype) {
+      case FAT_DTYPE_F16:
+        return dispatch_dim<__half, FAT_DTYPE_F16>(a, device, grid, ws);
+      case FAT_DTYPE_I8:
+        return dispatch_dim<__half, FAT_DTYPE_I8>(a, device, grid, ws);
+      case FAT_DTYPE_E4M3:
+        return dispatch_dim<__half, FAT_DTYPE_E4M3>(a, device, grid, ws);
+    }
+  } else {
+    switch (a.kv_dtype) {
+      case FAT_DTYPE_BF16:
+        return dispatch_dim<__nv_bfloat16, FAT_DTYPE_BF16>(a, device, grid, ws);
+      case FAT_DTYPE_I8:
+        return dispatch_dim<__nv_bfloat16, FAT_DTYPE_I8>(a, device, grid, ws);
+      case FAT_DTYPE_E4M3:
+        return dispatch_dim<__nv_bfloat16, FAT_DTYPE_E4M3>(a, device, grid, ws);
+    }
+  }
+  return unsupported("paged_decode: unsupported dtype combination");
+}
+
+}  // namespace fat

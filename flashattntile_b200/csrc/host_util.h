@@ -1,0 +1,34 @@
+// Host-side helpers shared by the C-ABI entry points: error reporting, device
+// properties and TMA tensor-map encoding through the driver entry point (so
+// the library does not link libcuda directly).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace fat {
+
+// Thread-local message behind fat_last_error().
+void set_last_error(const std::string& msg);
+const char* last_error();
+
+// Return FAT_ERR_INVALID_ARGUMENT with `msg` recorded.
+int invalid(const std::string& msg);
+int unsupported(const std::string& msg);
+int cuda_failure(const char* what, cudaError_t err);
+
+// Streaming-multiprocessor count of `device` (cached per device).
+int sm_count(int device);
+// Current device of the calling thread.
+int current_device();
+
+// cuTensorMapEncodeTiled resolved through cudaGetDriverEntryPoint.
+// dims/strides are innermost-first; strides[i] is the byte stride of dim i+1.
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle,
+                  std::string* why);
+
+}  // namespace fat

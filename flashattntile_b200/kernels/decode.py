@@ -1,0 +1,177 @@
+"""Paged decode attention on B200: launcher of the sm_100a decode kernel.
+
+Python API of FlashAttnTile's ``flashattn_tile/kernels/decode.py``:
+
+* ``paged_decode_attention(q, cache, softmax_scale=None, config=None, grouped=False)``
+  (``decode.py:533-642``)
+* ``paged_decode_attention_fp8(q, cache, scales, softmax_scale=None, config=None)``
+  (``decode.py:645-704``)
+* ``DEFAULT_CONFIG`` (``decode.py:458``)
+
+Both run the same CUDA kernel (``fat_paged_decode``): one persistent CTA per
+SM, pages split evenly over all SMs from ``seq_lens`` on the device, K/V
+pages staged by TMA once per GQA group, scores and P.V on the tensor cores
+with fp32 accumulation, INT8/e4m3 dequantised in registers.  ``split_k``,
+``num_warps``, ``num_stages`` and ``grouped`` are validated as in the
+reference and otherwise ignored: the split is chosen on the device and the
+result does not depend on them.
+
+There is no CPU or fp32 path: CPU tensors raise ``RuntimeError``; fp32
+queries raise ``NotImplementedError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _config, _lib
+from ..paging import PagedKVCache, validate_cache, validate_metadata
+
+DEFAULT_CONFIG = {"split_k": 1, "num_warps": 4, "num_stages": 2}
+# Import compatibility with code written against the reference: this build has
+# no Triton kernels; HAS_CUDA_KERNELS says whether the sm_100a library loads.
+HAS_TRITON = False
+HAS_CUDA_KERNELS = _lib.available()
+
+_QUANT_DTYPES = (torch.int8,) + ((torch.float8_e4m3fn,) if hasattr(torch, "float8_e4m3fn") else ())
+
+
+def _resolve_config(config: dict | None) -> dict:
+    """Key and range checks of ``decode.py:474-500`` (messages kept)."""
+    resolved = dict(DEFAULT_CONFIG)
+    if config is not None:
+        unknown = set(config) - set(DEFAULT_CONFIG)
+        if unknown:
+            raise ValueError(f"unknown decode config keys: {sorted(unknown)}")
+        resolved.update(config)
+    split_k = resolved["split_k"]
+    if not isinstance(split_k, int) or split_k < 1:
+        raise ValueError(f"split_k must be a positive integer, got {split_k}")
+    if split_k > 64:
+        raise ValueError(f"split_k must be <= 64, got {split_k}")
+    if resolved["num_warps"] not in (1, 2, 4, 8, 16, 32):
+        raise ValueError(f"num_warps must be a power of two <= 32, got {resolved['num_warps']}")
+    if resolved["num_stages"] < 1:
+        raise ValueError(f"num_stages must be >= 1, got {resolved['num_stages']}")
+    return resolved
+
+
+def _validate_decode_inputs(q: torch.Tensor, cache: PagedKVCache) -> None:
+    """``decode.py:503-522``: same checks, exception types and messages."""
+    if not isinstance(cache, PagedKVCache):
+        raise TypeError("cache must be a PagedKVCache")
+    if _config.validate_values():
+        validate_cache(cache)
+    else:
+        validate_metadata(cache)
+    if q.dim() != 3:
+        raise ValueError(f"q must be [batch, heads, head_dim], got {tuple(q.shape)}")
+    if q.shape[0] != cache.batch_size:
+        raise ValueError(f"q batch {q.shape[0]} != cache batch {cache.batch_size}")
+    if q.shape[2] != cache.head_dim:
+        raise ValueError(f"q head_dim {q.shape[2]} != cache head_dim {cache.head_dim}")
+    if q.shape[1] % cache.num_kv_heads != 0:
+        raise ValueError(f"num_heads {q.shape[1]} must be divisible by num_kv_heads {cache.num_kv_heads}")
+    if q.device != cache.k_cache.device:
+        raise ValueError("q and cache must live on the same device")
+    if not q.is_floating_point():
+        raise ValueError(f"q must be floating point, got {q.dtype}")
+    if _config.validate_values() and cache.batch_size and int(cache.seq_lens.min()) <= 0:
+        raise ValueError("decode requires every sequence to hold at least one cached token")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(
+                "flashattntile_b200 runs on CUDA tensors only; it has no CPU path "
+                f"(got a tensor on {t.device})")
+
+
+def _aligned_q(q: torch.Tensor) -> torch.Tensor:
+    eb = q.element_size()
+    ok = (q.stride(2) == 1 and q.data_ptr() % 16 == 0 and (q.stride(0) * eb) % 16 == 0
+          and (q.stride(1) * eb) % 16 == 0)
+    return q if ok else q.contiguous()
+
+
+def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
+                  k_scale=None, v_scale=None, out=None, out_dtype=None):
+    """Run ``fat_paged_decode`` on the current stream of q's device.
+
+    No host<->device synchronisation happens here; device-side problems are
+    recorded in the stream's error word (``flashattntile_b200.device_error``).
+    """
+    _require_cuda(q, k_cache, v_cache, page_table, seq_lens)
+    lib = _lib.load()
+    dev = q.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    q = _aligned_q(q)
+    if k_cache.stride() != v_cache.stride():
+        raise ValueError("k_cache and v_cache must have identical strides")
+    if k_cache.stride(3) != 1:
+        raise ValueError("k_cache/v_cache must be contiguous along head_dim")
+    if page_table.stride(1) != 1:
+        page_table = page_table.contiguous()
+    if not seq_lens.is_contiguous():
+        seq_lens = seq_lens.contiguous()
+    batch, heads, dim = q.shape
+    kvh = k_cache.shape[2]
+    out_dtype = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty((batch, heads, dim), dtype=out_dtype, device=dev)
+    scale_stride = 0
+    if k_scale is not None:
+        if k_scale.stride(1) != 1 or v_scale.stride() != k_scale.stride():
+            k_scale, v_scale = k_scale.contiguous(), v_scale.contiguous()
+        scale_stride = k_scale.stride(0)
+    with torch.cuda.device(idx):
+        ws_bytes = lib.fat_paged_decode_workspace_size(idx, batch, heads, kvh, dim)
+        ws = _lib.workspace(dev, ws_bytes)
+        err = _lib.error_word(dev)
+        status = lib.fat_paged_decode(
+            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+            k_cache.stride(1), k_cache.stride(2), k_cache.shape[0], page_table.data_ptr(), page_table.stride(0),
+            page_table.shape[1], seq_lens.data_ptr(), _lib.ptr(k_scale), _lib.ptr(v_scale), scale_stride,
+            out.data_ptr(), out.stride(0), out.stride(1), batch, heads, kvh, dim, int(page_size),
+            _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[k_cache.dtype], _lib.DTYPE_CODE[out_dtype],
+            float(softmax_scale), int(split_k), ws.data_ptr(), ws.numel(), err.data_ptr(),
+            _lib.stream_handle(dev))
+    _lib.check(status, "paged_decode")
+    return out
+
+
+def paged_decode_attention(q: torch.Tensor, cache: PagedKVCache, softmax_scale: float | None = None,
+                           config: dict | None = None, grouped: bool = False) -> torch.Tensor:
+    """One query per sequence against a paged fp16/bf16 cache -> ``[B, H, D]`` in q's dtype."""
+    _validate_decode_inputs(q, cache)
+    scale = float(softmax_scale) if softmax_scale is not None else q.shape[-1] ** -0.5
+    cfg = _resolve_config(config)
+    _require_cuda(q)
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"paged decode has fp16/bf16 kernels only, got {q.dtype}")
+    if cache.k_cache.dtype != q.dtype:
+        raise ValueError(f"q dtype {q.dtype} must match cache dtype {cache.k_cache.dtype}")
+    del grouped  # every launch shares each K/V page across its GQA group
+    return launch_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size,
+                         scale, cfg["split_k"])
+
+
+def paged_decode_attention_fp8(q: torch.Tensor, cache: PagedKVCache, scales, softmax_scale: float | None = None,
+                               config: dict | None = None) -> torch.Tensor:
+    """Decode against an INT8 / float8_e4m3fn cache with per-(page, KV-head) fp32 scales."""
+    _validate_decode_inputs(q, cache)
+    k_scale = scales["k"] if isinstance(scales, dict) else scales.k
+    v_scale = scales["v"] if isinstance(scales, dict) else scales.v
+    if cache.k_cache.dtype not in _QUANT_DTYPES:
+        raise ValueError(f"expected int8/float8 cache, got {cache.k_cache.dtype}")
+    expected = (cache.num_pages, cache.num_kv_heads)
+    if tuple(k_scale.shape) != expected or tuple(v_scale.shape) != expected:
+        raise ValueError(f"scales must have shape {expected}, got {tuple(k_scale.shape)}")
+    scale = float(softmax_scale) if softmax_scale is not None else q.shape[-1] ** -0.5
+    cfg = _resolve_config(config)
+    _require_cuda(q, k_scale, v_scale)
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"quantised decode requires fp16/bf16 queries, got {q.dtype}")
+    return launch_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size,
+                         scale, cfg["split_k"], k_scale=k_scale.float(), v_scale=v_scale.float())

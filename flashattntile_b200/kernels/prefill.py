@@ -1,0 +1,112 @@
+"""Packed varlen causal/non-causal prefill attention on B200.
+
+Python API of FlashAttnTile's ``flashattn_tile/kernels/prefill.py``:
+``prefill_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+max_seqlen_k, causal=True, softmax_scale=None, config=None)``
+(``prefill.py:236-326``) and ``DEFAULT_CONFIG`` (``prefill.py:145-150``).
+
+The launch goes to the sm_100a kernel ``fat_prefill_varlen`` (tcgen05 MMAs
+with accumulators in tensor memory, TMA-fed K/V).  ``config`` keys are
+validated as in the reference and otherwise ignored.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _config, _lib
+
+DEFAULT_CONFIG = {"BLOCK_M": 64, "BLOCK_N": 64, "num_warps": 4, "num_stages": 3}
+HAS_TRITON = False
+HAS_CUDA_KERNELS = _lib.available()
+
+
+def _resolve_config(config: dict | None) -> dict:
+    """``prefill.py:167-191`` without the persisted tuning lookup."""
+    resolved = dict(DEFAULT_CONFIG)
+    if config is not None:
+        unknown = set(config) - set(DEFAULT_CONFIG)
+        if unknown:
+            raise ValueError(f"unknown prefill config keys: {sorted(unknown)}")
+        resolved.update(config)
+    for key in ("BLOCK_M", "BLOCK_N"):
+        if resolved[key] <= 0 or resolved[key] & (resolved[key] - 1):
+            raise ValueError(f"{key} must be a positive power of two, got {resolved[key]}")
+    if resolved["num_warps"] not in (1, 2, 4, 8, 16, 32):
+        raise ValueError(f"num_warps must be a power of two <= 32, got {resolved['num_warps']}")
+    if resolved["num_stages"] < 1:
+        raise ValueError(f"num_stages must be >= 1, got {resolved['num_stages']}")
+    return resolved
+
+
+def _validate_inputs(q, k, v, cu_seqlens_q, cu_seqlens_k, causal) -> None:
+    """``prefill.py:194-233``: same checks, order and messages."""
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("q, k, v must be 3-D [tokens, heads, head_dim]")
+    if k.shape != v.shape:
+        raise ValueError(f"k shape {tuple(k.shape)} != v shape {tuple(v.shape)}")
+    if q.shape[-1] != k.shape[-1]:
+        raise ValueError(f"q head_dim {q.shape[-1]} != k head_dim {k.shape[-1]}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError(f"dtype mismatch: q {q.dtype}, k {k.dtype}, v {v.dtype}")
+    if not q.is_floating_point():
+        raise ValueError(f"expected floating point inputs, got {q.dtype}")
+    if q.device != k.device or k.device != v.device:
+        raise ValueError("q, k, v must live on the same device")
+    if cu_seqlens_q.dim() != 1 or cu_seqlens_k.dim() != 1:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must be 1-D")
+    if cu_seqlens_q.shape[0] != cu_seqlens_k.shape[0]:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must have the same batch dimension")
+    if cu_seqlens_q.numel() < 2:
+        raise ValueError("cu_seqlens must contain at least batch + 1 entries")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must be int32")
+    if cu_seqlens_q.device != q.device or cu_seqlens_k.device != q.device:
+        raise ValueError("cu_seqlens must live on the same device as q")
+    if _config.validate_values():
+        cq = cu_seqlens_q.tolist()
+        ck = cu_seqlens_k.tolist()
+        if cq[0] != 0 or ck[0] != 0:
+            raise ValueError("cu_seqlens must start at 0")
+        if cq[-1] != q.shape[0]:
+            raise ValueError("cu_seqlens_q[-1] must equal q.shape[0]")
+        if ck[-1] != k.shape[0]:
+            raise ValueError("cu_seqlens_k[-1] must equal k.shape[0]")
+        if any(b < a for a, b in zip(cq, cq[1:])):
+            raise ValueError("cu_seqlens_q must be non-decreasing")
+        if any(b < a for a, b in zip(ck, ck[1:])):
+            raise ValueError("cu_seqlens_k must be non-decreasing")
+        if causal and any((k1 - k0) < (q1 - q0) for q0, q1, k0, k1 in zip(cq, cq[1:], ck, ck[1:])):
+            raise ValueError("causal bottom-right alignment requires kv_len >= q_len per sequence")
+    if q.shape[1] % k.shape[1] != 0:
+        raise ValueError(f"num_heads ({q.shape[1]}) must be divisible by num_kv_heads ({k.shape[1]})")
+
+
+def launch_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal, softmax_scale,
+                   out=None, out_dtype=None):
+    """Run ``fat_prefill_varlen`` on the current stream (no host sync)."""
+    for t in (q, k, v, cu_seqlens_q, cu_seqlens_k):
+        if not t.is_cuda:
+            raise RuntimeError("flashattntile_b200 runs on CUDA tensors only; it has no CPU path")
+    lib = _lib.load()
+    if not hasattr(lib, "fat_prefill_varlen"):
+        raise NotImplementedError("this build of libflashattn_sm100.so has no prefill kernel")
+    raise NotImplementedError("prefill kernel not wired yet")
+
+
+def prefill_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, max_seqlen_k: int,
+                      causal: bool = True, softmax_scale: float | None = None, config: dict | None = None):
+    """Fused varlen prefill -> ``[total_q, num_heads, head_dim]`` in q's dtype."""
+    _validate_inputs(q, k, v, cu_seqlens_q, cu_seqlens_k, causal)
+    scale = float(softmax_scale) if softmax_scale is not None else q.shape[-1] ** -0.5
+    if max_seqlen_q <= 0:
+        raise ValueError(f"max_seqlen_q must be positive, got {max_seqlen_q}")
+    if max_seqlen_k <= 0:
+        raise ValueError(f"max_seqlen_k must be positive, got {max_seqlen_k}")
+    _resolve_config(config)
+    if not q.is_cuda:
+        raise RuntimeError("flashattntile_b200 runs on CUDA tensors only; it has no CPU path")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"prefill has fp16/bf16 kernels only, got {q.dtype}")
+    return launch_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q), int(max_seqlen_k), bool(causal),
+                          scale)

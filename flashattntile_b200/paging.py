@@ -1,0 +1,176 @@
+"""Paged KV-cache contract (NHD layout), same as FlashAttnTile's ``paging.py``.
+
+Layout (``flashattn_tile/paging.py:3-19``)
+------------------------------------------
+``k_cache`` / ``v_cache``
+    ``[num_pages, page_size, num_kv_heads, head_dim]``: page ``p`` holds
+    ``page_size`` consecutive tokens for every KV head.
+``page_table``
+    ``int32 [batch, max_pages_per_seq]``; entry ``[b, i]`` is the physical page
+    of logical block ``i`` of sequence ``b``.  Entries past a sequence's length
+    are never read.
+``seq_lens``
+    ``int32 [batch]``; token ``t`` of sequence ``b`` lives in page
+    ``page_table[b, t // page_size]`` at slot ``t % page_size``.
+
+``validate_cache`` keeps the reference's checks and ``AssertionError``
+messages (``paging.py:84-130``).  ``gather_paged`` runs a CUDA copy kernel
+(bit-exact, zero past each length) instead of the reference's per-sequence
+Python loop.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+
+@dataclass
+class PagedKVCache:
+    """Paged K/V cache plus its page table (``flashattn_tile/paging.py:30-76``)."""
+
+    k_cache: torch.Tensor
+    v_cache: torch.Tensor
+    page_table: torch.Tensor
+    seq_lens: torch.Tensor
+    page_size: int
+
+    @property
+    def batch_size(self) -> int:
+        return int(self.seq_lens.shape[0])
+
+    @property
+    def num_pages(self) -> int:
+        return int(self.k_cache.shape[0])
+
+    @property
+    def num_kv_heads(self) -> int:
+        return int(self.k_cache.shape[2])
+
+    @property
+    def head_dim(self) -> int:
+        return int(self.k_cache.shape[3])
+
+    @property
+    def max_pages_per_seq(self) -> int:
+        return int(self.page_table.shape[1])
+
+    @property
+    def capacity(self) -> int:
+        return self.max_pages_per_seq * self.page_size
+
+
+def _assert(condition: bool, message: str) -> None:
+    if not condition:
+        raise AssertionError(message)
+
+
+def validate_metadata(cache: PagedKVCache) -> None:
+    """Shape / dtype / device checks only: never reads device memory."""
+    _assert(isinstance(cache, PagedKVCache), "cache must be a PagedKVCache")
+    k, v = cache.k_cache, cache.v_cache
+    _assert(k.dim() == 4, f"k_cache must be 4-D [pages, page_size, kv_heads, dim], got {tuple(k.shape)}")
+    _assert(k.shape == v.shape, f"k_cache {tuple(k.shape)} and v_cache {tuple(v.shape)} must match")
+    _assert(k.dtype == v.dtype, f"k_cache dtype {k.dtype} != v_cache dtype {v.dtype}")
+    _assert(k.device == v.device, "k_cache and v_cache must live on the same device")
+    _assert(cache.page_size > 0, "page_size must be positive")
+    _assert(k.shape[1] == cache.page_size, f"k_cache page dim {k.shape[1]} != page_size {cache.page_size}")
+    _assert(cache.page_table.dtype == torch.int32, f"page_table must be int32, got {cache.page_table.dtype}")
+    _assert(cache.seq_lens.dtype == torch.int32, f"seq_lens must be int32, got {cache.seq_lens.dtype}")
+    _assert(cache.page_table.dim() == 2, "page_table must be [batch, max_pages_per_seq]")
+    _assert(cache.seq_lens.dim() == 1, "seq_lens must be [batch]")
+    _assert(cache.page_table.shape[0] == cache.seq_lens.shape[0], "page_table and seq_lens batch dimensions disagree")
+    _assert(cache.page_table.device == cache.seq_lens.device, "page_table and seq_lens must live on the same device")
+
+
+def validate_cache(cache: PagedKVCache, *, check_pages: bool = True) -> None:
+    """All checks of ``flashattn_tile/paging.py:84-130``, including the value
+    checks that read ``seq_lens`` / ``page_table`` back to the host."""
+    validate_metadata(cache)
+    if cache.seq_lens.numel() == 0:
+        return
+    lo, hi = torch.aminmax(cache.seq_lens)
+    _assert(int(lo) >= 0, "seq_lens must be non-negative")
+    max_len = int(hi)
+    _assert(max_len <= cache.capacity, f"seq_len {max_len} exceeds page-table capacity {cache.capacity}")
+    if check_pages and max_len > 0:
+        used = cache.page_table[:, : math.ceil(max_len / cache.page_size)]
+        umin, umax = torch.aminmax(used)
+        _assert(int(umin) >= 0, "page_table contains a negative page id")
+        _assert(int(umax) < cache.num_pages,
+                f"page_table references page {int(umax)} but cache has {cache.num_pages} pages")
+
+
+def allocate(batch: int, max_seq_len: int, num_kv_heads: int, head_dim: int, page_size: int,
+             dtype: torch.dtype = torch.float16, device: torch.device | str = "cuda") -> PagedKVCache:
+    """Zeroed cache with a contiguous page mapping (``paging.py:133-169``)."""
+    _assert(batch > 0, "batch must be positive")
+    _assert(max_seq_len > 0, "max_seq_len must be positive")
+    _assert(num_kv_heads > 0 and head_dim > 0, "num_kv_heads and head_dim must be positive")
+    _assert(page_size > 0, "page_size must be positive")
+    allowed = {torch.float16, torch.bfloat16, torch.float32, torch.int8}
+    if hasattr(torch, "float8_e4m3fn"):
+        allowed.add(torch.float8_e4m3fn)
+    _assert(dtype in allowed, f"unsupported cache dtype {dtype}")
+    pages_per_seq = math.ceil(max_seq_len / page_size)
+    num_pages = batch * pages_per_seq
+    k_cache = torch.zeros((num_pages, page_size, num_kv_heads, head_dim), dtype=dtype, device=device)
+    cache = PagedKVCache(
+        k_cache=k_cache,
+        v_cache=torch.zeros_like(k_cache),
+        page_table=torch.arange(num_pages, dtype=torch.int32, device=device).reshape(batch, pages_per_seq),
+        seq_lens=torch.zeros(batch, dtype=torch.int32, device=device),
+        page_size=page_size,
+    )
+    validate_cache(cache)
+    return cache
+
+
+def append_tokens(cache: PagedKVCache, new_k: torch.Tensor, new_v: torch.Tensor) -> None:
+    """Append one token per sequence in place (``paging.py:172-210``)."""
+    validate_metadata(cache)
+    shape = (cache.batch_size, cache.num_kv_heads, cache.head_dim)
+    _assert(new_k.shape == shape, f"new_k must be [{shape[0]}, {shape[1]}, {shape[2]}], got {tuple(new_k.shape)}")
+    _assert(new_v.shape == new_k.shape, f"new_v shape {tuple(new_v.shape)} != new_k shape {tuple(new_k.shape)}")
+    _assert(new_k.dtype == cache.k_cache.dtype, f"new_k dtype {new_k.dtype} != cache dtype {cache.k_cache.dtype}")
+    _assert(new_v.dtype == cache.k_cache.dtype, f"new_v dtype {new_v.dtype} != cache dtype {cache.k_cache.dtype}")
+    _assert(new_k.device == cache.k_cache.device, "new_k must be on the cache device")
+    _assert(new_v.device == cache.k_cache.device, "new_v must be on the cache device")
+    positions = cache.seq_lens.long()
+    _assert(int(positions.max()) < cache.capacity, f"append would exceed page-table capacity {cache.capacity}")
+    page_idx = torch.div(positions, cache.page_size, rounding_mode="floor")
+    rows = torch.arange(cache.batch_size, device=cache.page_table.device)
+    phys = cache.page_table[rows, page_idx.to(cache.page_table.device)].long()
+    pmin, pmax = torch.aminmax(phys)
+    _assert(int(pmin) >= 0 and int(pmax) < cache.num_pages,
+            f"page_table maps to a page outside [0, {cache.num_pages})")
+    phys = phys.to(cache.k_cache.device)
+    slots = (positions % cache.page_size).to(cache.k_cache.device)
+    cache.k_cache[phys, slots] = new_k
+    cache.v_cache[phys, slots] = new_v
+    cache.seq_lens += 1
+
+
+def gather_paged(k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor, seq_lens: torch.Tensor,
+                 page_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Padded contiguous ``[batch, max_len, kv_heads, dim]`` copies, zero past each
+    length (``paging.py:213-256``), produced by the CUDA gather kernel."""
+    _assert(k_cache.shape == v_cache.shape, "k_cache and v_cache shapes must match")
+    _assert(page_table.dtype == torch.int32, "page_table must be int32")
+    _assert(seq_lens.dtype == torch.int32, "seq_lens must be int32")
+    _assert(page_table.dim() == 2 and seq_lens.dim() == 1, "expected page_table [B, P] and seq_lens [B]")
+    _assert(page_table.shape[0] == seq_lens.shape[0], "page_table / seq_lens batch mismatch")
+    _assert(k_cache.shape[1] == page_size, "k_cache page dim != page_size")
+    from .kernels.gather import gather_paged_cuda
+
+    return gather_paged_cuda(k_cache, v_cache, page_table, seq_lens, page_size)
+
+
+def gather_contiguous(cache: PagedKVCache) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gather ``cache`` into padded contiguous K/V (``paging.py:259-262``)."""
+    validate_cache(cache)
+    return gather_paged(cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size)

@@ -1,0 +1,117 @@
+/*
+ * flashattn_tile_b200 -- C ABI of the B200 (sm_100a) paged-attention library.
+ *
+ * Every entry point takes raw device pointers, element strides (in elements,
+ * the innermost dimension must be contiguous), plain integer sizes and a
+ * cudaStream_t passed as void*.  Nothing here allocates device memory except
+ * where a function says so; scratch space is passed in by the caller.
+ *
+ * Each function returns a fat_status.  On failure fat_last_error() holds a
+ * message for the calling thread.  Kernels that can detect a problem only on
+ * the device (a page id outside the pool, a pipeline wait that timed out)
+ * OR a FAT_DEVERR_* bit into the caller's int32 device error word and
+ * finish without faulting; the caller reads the word when it wants to know.
+ *
+ * Reference interface replaced (FlashAttnTile, path:line in that project):
+ *   fat_paged_decode          flashattn_tile/ops.py:35-55 (flashattn_tile::paged_decode),
+ *                             kernels/decode.py:533-642 (paged_decode_attention),
+ *                             kernels/decode.py:645-704 (paged_decode_attention_fp8),
+ *                             csrc/paged_decode.cu:297-344 (paged_decode_cuda)
+ *   fat_prefill_varlen        flashattn_tile/ops.py:76-99 (flashattn_tile::prefill_varlen),
+ *                             kernels/prefill.py:236-326 (prefill_attention)
+ *   fat_gather_paged          flashattn_tile/paging.py:213-256 (gather_paged)
+ *   fat_lse_merge             kernels/decode.py:316-356 (_decode_reduce_kernel)
+ */
+#ifndef FLASHATTN_TILE_B200_H_
+#define FLASHATTN_TILE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+enum {
+  FAT_OK = 0,
+  FAT_ERR_INVALID_ARGUMENT = 1, /* shapes, strides, pointers or values are inconsistent */
+  FAT_ERR_UNSUPPORTED = 2,      /* a valid request this build has no kernel for       */
+  FAT_ERR_CUDA = 3,             /* a CUDA runtime call or kernel launch failed         */
+  FAT_ERR_WORKSPACE = 4         /* the scratch buffer passed in is too small           */
+};
+
+/* Bits OR-ed into the device error word. */
+enum {
+  FAT_DEVERR_TIMEOUT = 1,  /* a bounded pipeline wait gave up; the output is invalid  */
+  FAT_DEVERR_BAD_PAGE = 2  /* a page id used by a sequence is outside [0, num_pages) */
+};
+
+/* Element types. */
+enum {
+  FAT_DTYPE_F16 = 0,
+  FAT_DTYPE_BF16 = 1,
+  FAT_DTYPE_F32 = 2,
+  FAT_DTYPE_I8 = 3,  /* symmetric int8 with per-(page, kv head) fp32 scales */
+  FAT_DTYPE_E4M3 = 4 /* float8_e4m3fn with per-(page, kv head) fp32 scales  */
+};
+
+/* Library version string, e.g. "flashattn_tile_b200 0.1.0 sm_100a". */
+const char* fat_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* fat_last_error(void);
+
+/*
+ * Bytes of scratch fat_paged_decode needs for this problem on `device`.
+ * The caller zero-fills the buffer once; every successful call leaves it
+ * zero-filled again, so one buffer serves any number of calls that are
+ * ordered on one stream.
+ */
+size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int num_kv_heads, int head_dim);
+
+/*
+ * Single-query paged decode: out[b, h, :] = softmax(scale * q[b, h] . K^T) V over
+ * the seq_lens[b] cached tokens of sequence b, K/V read through the page table
+ * (token t in page page_table[b, t / page_size], slot t % page_size), query head
+ * h reading KV head h / (num_heads / num_kv_heads).
+ *
+ *   q          [batch, num_heads, head_dim]          q_dtype (F16 | BF16)
+ *   k/v_cache  [num_pages, page_size, num_kv_heads, head_dim]
+ *              kv_dtype = q_dtype, or I8 / E4M3 with k/v_scale [num_pages, num_kv_heads] fp32
+ *   page_table int32 [batch, >= ceil(max seq_len / page_size)]
+ *   seq_lens   int32 [batch]; a sequence of length 0 produces zeros
+ *   out        [batch, num_heads, head_dim]          out_dtype (= q_dtype, or F32)
+ *
+ * head_dim in {64, 128, 256}; page_size 8 or a multiple of 16 up to 256; K/V
+ * base addresses 16-byte aligned and their page/slot/head strides multiples of
+ * 16 bytes.  split_k_hint (1..64) is accepted for interface compatibility: the
+ * kernel chooses its own balanced split of the pages over all SMs, and the
+ * result does not depend on it.
+ */
+int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
+                     const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                     int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                     const int32_t* seq_lens, const float* k_scale, const float* v_scale,
+                     int64_t scale_stride_page, void* out, int64_t out_stride_b, int64_t out_stride_h, int batch,
+                     int num_heads, int num_kv_heads, int head_dim, int page_size, int q_dtype, int kv_dtype,
+                     int out_dtype, float softmax_scale, int split_k_hint, void* workspace, size_t workspace_bytes,
+                     int32_t* error_word, void* stream);
+
+/*
+ * Page-table gather: out_k/out_v [batch, max_len, num_kv_heads, row_bytes] (contiguous)
+ * receive, bit for bit, the rows of each sequence's first seq_lens[b] tokens, and
+ * zeros past that.  The cache is addressed by byte strides (page, slot, head); the
+ * element type does not matter (row_bytes = head_dim * element size).
+ */
+int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_page_bytes, int64_t stride_slot_bytes,
+                     int64_t stride_head_bytes, int64_t num_pages, const int32_t* page_table,
+                     int64_t page_table_stride, int64_t max_pages, const int32_t* seq_lens, void* out_k, void* out_v,
+                     int64_t max_len, int batch, int num_kv_heads, int page_size, int64_t row_bytes,
+                     int32_t* error_word, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHATTN_TILE_B200_H_ */
