@@ -664,11 +664,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
         const long long unit = (long long)b * nkg + unit_local;
+        // The pieces of this unit belong to the CTAs whose (non-empty) chunk
+        // ranges overlap it: owner(first chunk) .. owner(last chunk), skipping
+        // CTAs with empty ranges (there are more CTAs than chunks when the
+        // problem is small).
         const int ca = int(owner_of(unit_base, total, gridDim.x));
         const int cb = int(owner_of(unit_base + chunks_b - 1, total, gridDim.x));
         if (ctid == 0) {
+          int parts = 0;
+          for (int cc = ca; cc <= cb; ++cc)
+            parts += range_start(cc + 1, total, gridDim.x) > range_start(cc, total, gridDim.x) ? 1 : 0;
           const int ticket = atomicAdd(p.ws_count + unit, 1);
-          shi[1] = (ticket == cb - ca) ? 1 : 0;
+          shi[1] = (ticket == parts - 1) ? 1 : 0;
         }
         if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
         if (shi[1]) {
@@ -677,12 +684,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int gg = idx / D, d = idx - gg * D;
             float M = -CUDART_INF_F;
             for (int cc = ca; cc <= cb; ++cc) {
-              const int sl = (range_start(cc, total, gridDim.x) < unit_base) ? 1 : 0;
+              const long long rs = range_start(cc, total, gridDim.x);
+              if (range_start(cc + 1, total, gridDim.x) == rs) continue;
+              const int sl = (rs < unit_base) ? 1 : 0;
               M = fmaxf(M, __ldcg(p.ws_ml + (((long long)cc * 2 + sl) * kRows + gg) * 2));
             }
             float Lsum = 0.f, O = 0.f;
             for (int cc = ca; cc <= cb; ++cc) {
-              const int sl = (range_start(cc, total, gridDim.x) < unit_base) ? 1 : 0;
+              const long long rs = range_start(cc, total, gridDim.x);
+              if (range_start(cc + 1, total, gridDim.x) == rs) continue;
+              const int sl = (rs < unit_base) ? 1 : 0;
               const long long base = ((long long)cc * 2 + sl) * kRows + gg;
               const float wt = fast_exp2(__ldcg(p.ws_ml + base * 2) - M);
               Lsum += __ldcg(p.ws_ml + base * 2 + 1) * wt;
