@@ -698,6 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float wt = fast_exp2(__ldcg(p.ws_ml + base * 2) - M);
               Lsum += __ldcg(p.ws_ml + base * 2 + 1) * wt;
               O += __ldcg(p.ws_o + base * D + d) * wt;
+              __stcg(p.ws_o + base * D + d, 0.f);  // only this thread reads this entry
             }
             const long long off = (long long)b * p.o_sb + (long long)(h0 + gg) * p.o_sh + d;
             const float val = O / Lsum;
@@ -707,7 +708,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
             }
           }
-          if (ctid == 0) p.ws_count[unit] = 0;  // leave the ticket zeroed for the next call
+          // Leave the whole workspace zero-filled for the next call, whatever
+          // its shape: the (m, l) pairs once every thread has read them, then
+          // the ticket.
+          if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
+          for (int cc = ca + ctid / kRows; cc <= cb; cc += (kWarps * 32) / kRows) {
+            const int gg = ctid % kRows;
+            const long long rs = range_start(cc, total, gridDim.x);
+            if (gg >= rows || range_start(cc + 1, total, gridDim.x) == rs) continue;
+            const long long base = ((long long)cc * 2 + ((rs < unit_base) ? 1 : 0)) * kRows + gg;
+            __stcg(p.ws_ml + base * 2, 0.f);
+            __stcg(p.ws_ml + base * 2 + 1, 0.f);
+          }
+          if (ctid == 0) p.ws_count[unit] = 0;
         }
       }
       if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;

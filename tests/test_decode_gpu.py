@@ -149,6 +149,21 @@ def test_repeated_calls_reuse_the_workspace():
     _no_device_error()
 
 
+def test_workspace_is_left_zero_across_shapes():
+    """Split merges across shapes share one scratch buffer; it must come back zero-filled."""
+    from flashattntile_b200 import _lib
+
+    cases = [([3000, 17, 900], 8, 2, 128, 16), ([1, 17, 255, 1000], 64, 8, 64, 8), ([20000], 8, 1, 256, 64),
+             ([400] * 40, 16, 4, 64, 16)]
+    for lens, h, hkv, d, ps in cases * 2:
+        q, k, v, table, lens_t = paged_case(33 + d, lens, h, hkv, d, ps)
+        out32 = _run(q, k, v, table, lens_t, ps, out_dtype=torch.float32)
+        assert_close_f32(out32, _oracle(q, k, v, table, lens_t, ps, torch.float16, out_f32=True), atol=1e-4)
+        for buf in _lib._WS.values():
+            assert int(torch.count_nonzero(buf)) == 0
+    _no_device_error()
+
+
 def test_garbage_past_sequence_end_is_ignored():
     q, k, v, table, lens = paged_case(28, [5, 17, 33], 8, 2, 64, 16)
     clean = _run(q, k, v, table, lens, 16, out_dtype=torch.float32)
