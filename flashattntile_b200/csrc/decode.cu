@@ -44,6 +44,19 @@ constexpr int kStageBudget = 160 * 1024;   // shared memory for the stage ring
 
 enum : int { kFirst = 1, kLast = 2, kFull = 4, kDone = 8 };
 
+// Producer lookahead: page ids are fetched kPF chunks ahead of the stage being
+// filled and 8-bit scales kPF2 chunks ahead, through a ring of kRing slots.
+constexpr int kPF = 6;
+constexpr int kPF2 = 3;
+constexpr int kRing = 8;
+static_assert(kRing > kPF && kPF > kPF2 && kPF2 > 0, "prefetch ring too small");
+
+struct RingInfo {
+  int b, unit_local, chunk, len, chunks_b, nbox;
+  long long S;
+};
+constexpr int kRingBytes = kRing * int(sizeof(RingInfo)) + kRing * 8 * 4 * 3;
+
 struct Meta {
   int flags;
   int b;
@@ -88,7 +101,7 @@ struct Layout {
   static constexpr int kMergeFloats = kWarps * kRows * (D + 8) + 2 * kWarps * kRows;
   static constexpr size_t kSmem = 1024 /*align slack*/ + size_t(kStages) * kStage + size_t(kStages) * kQBytes +
                                   size_t(kStages) * sizeof(Meta) + size_t(kMergeFloats) * 4 +
-                                  size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16;
+                                  size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16 + kRingBytes + 16;
 
   // Shared address of byte column `bc` (multiple of 16) of token row `row` of a tile.
   static __device__ __forceinline__ uint32_t addr(uint32_t tile, int row, int bc) {
@@ -200,6 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 1);  // [0] abort [1] last-flag
   long long* shl = reinterpret_cast<long long*>(const_cast<int*>(shi) + 4);   // [0] start_b [1] start_S [2] total
   long long* scan = shl + 4;                                                    // [kThreads]
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(scan + kThreads) + 15) & ~uintptr_t(15));     // producer prefetch ring
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -282,17 +297,101 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
     }
+    // The walk over this CTA's chunks runs kPF chunks ahead of the stage
+    // being filled: for each future chunk it records the unit info in a small
+    // shared ring and starts cp.async copies of its page ids (and, for 8-bit
+    // caches, kPF2 chunks ahead, of the pages' scales), so the TMA issue for
+    // a stage never waits on a dependent global load.
     int it = 0;
+    RingInfo* rinfo = reinterpret_cast<RingInfo*>(ring_base);
+    int* rids = reinterpret_cast<int*>(rinfo + kRing);
+    float* rks = reinterpret_cast<float*>(rids + kRing * 8);
+    float* rvs = rks + kRing * 8;
     if (x0 < x1) {
-      int b = int(shl[0]);
-      long long S = shl[1];
-      int len = max(__ldg(p.seq_lens + b), 0);
-      int chunks_b = (len + kChunk - 1) / kChunk;
-      long long pos = x0 - S * nkg;
+      int wb = int(shl[0]);
+      long long wS = shl[1];
+      int wlen = max(__ldg(p.seq_lens + wb), 0);
+      int wchunks = (wlen + kChunk - 1) / kChunk;
+      long long wpos = x0 - wS * nkg;
+      long long xl = x0;
+      auto prefetch_ids = [&]() {
+        if (xl < x1) {
+          const int r = int((xl - x0) % kRing);
+          const int unit_local = int(wpos / wchunks);
+          const int chunk = int(wpos - (long long)unit_local * wchunks);
+          const int tok0 = chunk * kChunk;
+          const int nbox = (min(kChunk, wlen - tok0) + p.box_rows - 1) / p.box_rows;
+          if (lane == 0) {
+            rinfo[r].b = wb;
+            rinfo[r].unit_local = unit_local;
+            rinfo[r].chunk = chunk;
+            rinfo[r].len = wlen;
+            rinfo[r].chunks_b = wchunks;
+            rinfo[r].nbox = nbox;
+            rinfo[r].S = wS;
+          }
+          if (lane < nbox) {
+            const int lp = (tok0 + lane * p.box_rows) / p.page_size;
+            int* dst = rids + r * 8 + lane;
+            if (lp < p.max_pages) {
+              cp_async_4(smem_u32(dst), p.page_table + (long long)wb * p.pt_sb + lp);
+            } else {
+              *dst = -1;
+            }
+          }
+          ++xl;
+          ++wpos;
+          if (wpos == (long long)wchunks * nkg && xl < x1) {
+            wS += wchunks;
+            wpos = 0;
+            do {
+              ++wb;
+              wlen = max(__ldg(p.seq_lens + wb), 0);
+              wchunks = (wlen + kChunk - 1) / kChunk;
+            } while (wchunks == 0 && wb + 1 < p.batch);
+          }
+        }
+        cp_async_commit();
+      };
+      // Scales of chunk xs (its page ids must have landed): 8-bit caches only.
+      auto prefetch_scales = [&](long long xs) {
+        if constexpr (EB == 1) {
+          if (xs >= x0 && xs < x1) {
+            const int r = int((xs - x0) % kRing);
+            const int nbox = rinfo[r].nbox;
+            const int kvh = rinfo[r].unit_local / p.head_groups;
+            if (lane < nbox) {
+              const int ph = rids[r * 8 + lane];
+              if (ph >= 0 && ph < p.num_pages) {
+                cp_async_4(smem_u32(rks + r * 8 + lane), p.k_scale + (long long)ph * p.s_sp + kvh);
+                cp_async_4(smem_u32(rvs + r * 8 + lane), p.v_scale + (long long)ph * p.s_sp + kvh);
+              }
+            }
+          }
+        }
+        cp_async_commit();
+      };
+      // Step k commits two groups: page ids of chunk x0+k, then scales of
+      // chunk x0+k-(kPF-kPF2) (empty for 16-bit caches).  Before issuing the
+      // scales of chunk y we need y's ids: 2*(kPF-kPF2) groups were committed
+      // after them.  Before filling the stage of chunk x (step x-x0+kPF) we
+      // need x's scales: 2*kPF2 groups were committed after them.
+      auto step = [&](long long k) {
+        prefetch_ids();
+        cp_async_wait<2 * (kPF - kPF2)>();
+        __syncwarp();
+        prefetch_scales(x0 + k - (kPF - kPF2));
+      };
+      for (int k = 0; k < kPF; ++k) step(k);
       bool full_seg = false;
       for (long long x = x0; x < x1; ++x) {
-        const int unit_local = int(pos / chunks_b);
-        const int chunk = int(pos - (long long)unit_local * chunks_b);
+        step(x - x0 + kPF);
+        cp_async_wait<2 * kPF2>();
+        __syncwarp();
+        const int r = int((x - x0) % kRing);
+        const int b = rinfo[r].b, unit_local = rinfo[r].unit_local, chunk = rinfo[r].chunk;
+        const int len = rinfo[r].len, chunks_b = rinfo[r].chunks_b, nbox = rinfo[r].nbox;
+        const long long S = rinfo[r].S;
         const bool first = (x == x0) || chunk == 0;
         const bool last = (x == x1 - 1) || chunk == chunks_b - 1;
         if (first) full_seg = (chunk == 0) && (x1 - x >= chunks_b);
@@ -303,13 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kvh = unit_local / p.head_groups;
         const int hg = unit_local - kvh * p.head_groups;
         const int tok0 = chunk * kChunk;
-        const int valid = min(kChunk, len - tok0);
-        const int nbox = (valid + p.box_rows - 1) / p.box_rows;
         int phys = -1;
         if (lane < nbox) {
-          const int t = tok0 + lane * p.box_rows;
-          const int lp = t / p.page_size;
-          phys = lp < p.max_pages ? __ldg(p.page_table + (long long)b * p.pt_sb + lp) : -1;
+          phys = rids[r * 8 + lane];
           if (phys < 0 || phys >= p.num_pages) {
             raise_error(p.err, FAT_DEVERR_BAD_PAGE);
             phys = -1;
@@ -321,11 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // One scale pair per 8-token group of the chunk; groups past the
           // sequence end (or on a rejected page) get 0 so that masked tokens
           // never meet stale shared memory.
-          float ksc = 0.f, vsc = 0.f;
-          if (phys >= 0) {
-            ksc = __ldg(p.k_scale + (long long)phys * p.s_sp + kvh);
-            vsc = __ldg(p.v_scale + (long long)phys * p.s_sp + kvh);
-          }
+          const float ksc = phys >= 0 ? rks[r * 8 + lane] : 0.f;
+          const float vsc = phys >= 0 ? rvs[r * 8 + lane] : 0.f;
           const int per8 = p.box_rows / 8;  // 8-token groups per box
           const int src = (lane & 7) / per8;
           const float kg = __shfl_sync(0xffffffffu, ksc, src);
@@ -382,19 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         ++it;
-        ++pos;
-        if (pos == (long long)chunks_b * nkg && x + 1 < x1) {
-          // advance to the next sequence with cached tokens
-          S += chunks_b;
-          pos = 0;
-          do {
-            ++b;
-            len = max(__ldg(p.seq_lens + b), 0);
-            chunks_b = (len + kChunk - 1) / kChunk;
-          } while (chunks_b == 0 && b + 1 < p.batch);
-        }
       }
     }
+    cp_async_wait<0>();
     // Termination marker (or, after an abort, drain this CTA's own copies).
     if (!*abort_flag) {
       const int s = it % kStages;
