@@ -5,6 +5,7 @@
 
 #include "decode.h"
 #include "gather.h"
+#include "prefill.h"
 #include "host_util.h"
 
 extern "C" {
@@ -62,6 +63,45 @@ int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, cons
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
   return fat::launch_paged_decode(a);
+}
+
+int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                       int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, void* out,
+                       int64_t out_stride_t, int64_t out_stride_h, const int32_t* cu_seqlens_q,
+                       const int32_t* cu_seqlens_k, int batch, int64_t total_q, int64_t total_k, int num_heads,
+                       int num_kv_heads, int head_dim, int max_seqlen_q, int max_seqlen_k, int causal,
+                       float softmax_scale, int dtype, int out_dtype, int32_t* error_word, void* stream) {
+  fat::set_last_error("");
+  fat::PrefillArgs a;
+  a.q = q;
+  a.q_st = q_stride_t;
+  a.q_sh = q_stride_h;
+  a.k = k;
+  a.k_st = k_stride_t;
+  a.k_sh = k_stride_h;
+  a.v = v;
+  a.v_st = v_stride_t;
+  a.v_sh = v_stride_h;
+  a.out = out;
+  a.o_st = out_stride_t;
+  a.o_sh = out_stride_h;
+  a.cu_q = cu_seqlens_q;
+  a.cu_k = cu_seqlens_k;
+  a.batch = batch;
+  a.total_q = total_q;
+  a.total_k = total_k;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.max_seqlen_q = max_seqlen_q;
+  a.max_seqlen_k = max_seqlen_k;
+  a.causal = causal;
+  a.softmax_scale = softmax_scale;
+  a.dtype = dtype;
+  a.out_dtype = out_dtype;
+  a.error_word = error_word;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return fat::launch_prefill_varlen(a);
 }
 
 int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_page_bytes, int64_t stride_slot_bytes,

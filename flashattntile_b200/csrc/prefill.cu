@@ -1,0 +1,443 @@
+// Packed varlen prefill attention (causal or not, GQA/MQA) for sm_100a.
+//
+// Replaces FlashAttnTile's _fwd_varlen_kernel (flashattn_tile/kernels/prefill.py:34-138):
+// per (128-row query tile, query head, sequence) an online-softmax pass over
+// 128-row K/V tiles with bottom-right causal alignment (query i sees keys
+// j <= i + kv_len - q_len), GQA head h reading KV head h / G, P rounded to the
+// input dtype before P.V (prefill.py:128) and fp32 accumulation.
+//
+// One CTA per query tile, warp-specialised:
+//   warp 4      TMA producer: the Q tile once, then K and V tiles into two
+//               independent 128-byte-swizzled rings (K released after Q.K^T,
+//               V after P.V);
+//   warp 5      tcgen05 issuer (one thread): S_j = Q K_j^T into one of two
+//               tensor-memory S buffers, then O += P_{j-1} V_{j-1} with P read
+//               straight from tensor memory, so the next Q.K^T overlaps the
+//               softmax of the previous tile;
+//   warps 0-3   softmax: thread r owns query row r (tensor-memory lane r), reads
+//               its S row, keeps the running max and sum in registers, writes P
+//               (16-bit) over its S row, and rescales O in tensor memory only
+//               when the row max grew by more than 2^8 (P stays <= 256).
+// Accumulators live in tensor memory: S0, S1 (128 columns each) and O (head_dim
+// columns).  Every wait is bounded; on a timeout the CTA records
+// FAT_DEVERR_TIMEOUT, drains its copies and MMAs, frees tensor memory and exits.
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "host_util.h"
+#include "prefill.h"
+#include "tcgen05.cuh"
+
+namespace fat {
+namespace pre {
+
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // keys per K/V tile
+constexpr int kSoftmaxWarps = 4;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 6 * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 without rescaling
+
+struct Params {
+  const int* cu_q;
+  const int* cu_k;
+  void* out;
+  long long o_st, o_sh;
+  int num_heads, group;
+  float scale_log2;
+  int causal;
+  int out_f32;
+  int* err;
+};
+
+template <int D>
+struct Layout {
+  static constexpr int kCB = D / 64;            // 128-byte column blocks (16-bit elements)
+  static constexpr int kTile = BM * D * 2;      // one Q, K or V tile
+  static constexpr int kStagesK = D <= 64 ? 4 : 3;
+  static constexpr int kStagesV = D <= 64 ? 4 : 3;
+  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 + 2 + 3) + 16;
+  static constexpr size_t kSmem = 1024 + size_t(kTile) * (1 + kStagesK + kStagesV) + kBarBytes;
+  static constexpr uint32_t kColS = 0;    // S_b at column kColS + 128 b
+  static constexpr uint32_t kColO = 256;  // O at columns [256, 256 + D)
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using L = Layout<D>;
+  constexpr int SK = L::kStagesK, SV = L::kStagesV;
+  constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t kIdescQK = tc::idesc_f16(BM, BN, fmt, 0, 0);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(BM, D, fmt, 0, 1);
+
+  const int h = blockIdx.x % p.num_heads;
+  const int b = blockIdx.x / p.num_heads;
+  const int m_tile = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
+  const int q0 = __ldg(p.cu_q + b), q_len = __ldg(p.cu_q + b + 1) - q0;
+  const int k0 = __ldg(p.cu_k + b), kv_len = __ldg(p.cu_k + b + 1) - k0;
+  const int m0 = m_tile * BM;
+  if (m0 >= q_len) return;  // uniform for the CTA, before any barrier or allocation
+  const int kvh = h / p.group;
+  const int offset = kv_len - q_len;  // bottom-right causal alignment
+  int n_kv = kv_len > 0 ? (kv_len + BN - 1) / BN : 0;
+  if (p.causal) {
+    const int lim = min(m0 + BM, q_len) - 1 + offset;  // last key any row of the tile sees
+    n_kv = lim < 0 ? 0 : min(n_kv, lim / BN + 1);
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK = sQ + L::kTile;
+  const uint32_t sV = sK + SK * L::kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(L::kTile) * (1 + SK + SV));
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t q_full = bar0;
+  const uint32_t k_full = bar0 + 8;                 // [SK]
+  const uint32_t k_empty = k_full + 8 * SK;         // [SK]
+  const uint32_t v_full = k_empty + 8 * SK;         // [SV]
+  const uint32_t v_empty = v_full + 8 * SV;         // [SV]
+  const uint32_t s_full = v_empty + 8 * SV;         // [2]
+  const uint32_t p_full = s_full + 16;              // [2]
+  const uint32_t o_done = p_full + 16;              // PV completions
+  const uint32_t o_final = o_done + 8;              // after the last P.V
+  const uint32_t drain = o_final + 8;               // final MMA drain
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < SK; ++s) {
+      mbar_init(k_full + 8 * s, 1);
+      mbar_init(k_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < SV; ++s) {
+      mbar_init(v_full + 8 * s, 1);
+      mbar_init(v_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(s_full + 8 * s, 1);
+      mbar_init(p_full + 8 * s, kSoftmaxWarps * 32);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    // ============================ TMA producer ============================
+    int issued_k = 0, issued_v = 0;
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(q_full, L::kTile);
+#pragma unroll
+      for (int cb = 0; cb < L::kCB; ++cb) tma_load_3d(sQ + cb * BM * 128, &tm_q, q_full, cb * 64, h, q0 + m0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int sk = j % SK, sv = j % SV;
+        if (!mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
+#pragma unroll
+        for (int cb = 0; cb < L::kCB; ++cb)
+          tma_load_3d(sK + sk * L::kTile + cb * BN * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, k0 + j * BN);
+        ++issued_k;
+        if (!mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full + 8 * sv, L::kTile);
+#pragma unroll
+        for (int cb = 0; cb < L::kCB; ++cb)
+          tma_load_3d(sV + sv * L::kTile + cb * BN * 128, &tm_v, v_full + 8 * sv, cb * 64, kvh, k0 + j * BN);
+        ++issued_v;
+      }
+      if (*abort_flag) {
+        // Drain this CTA's own copies before the shared memory goes away.
+        mbar_wait_bounded(q_full, 0, nullptr, nullptr);
+        for (int j = max(0, issued_k - SK); j < issued_k; ++j)
+          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr);
+        for (int j = max(0, issued_v - SV); j < issued_v; ++j)
+          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ============================ MMA issuer ============================
+    if (lane == 0 && n_kv > 0) {
+      auto issue_pv = [&](int i) -> bool {
+        const int sb = i & 1, sv = i % SV;
+        if (!mbar_wait_bounded(p_full + 8 * sb, (i >> 1) & 1, p.err, abort_flag)) return false;
+        if (!mbar_wait_bounded(v_full + 8 * sv, (i / SV) & 1, p.err, abort_flag)) return false;
+        tc::fence_after_sync();
+        const uint32_t vbase = sV + sv * L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bdesc = tc::sdesc_sw128(vbase + kk * 16 * 128, BN * 128, 1024);
+          tc::mma_ts(tmem + L::kColO, tmem + L::kColS + 128 * sb + kk * 8, bdesc, kIdescPV,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(v_empty + 8 * sv);
+        tc::commit(o_done);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, p.err, abort_flag);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int sb = j & 1, sk = j % SK;
+        if (!mbar_wait_bounded(k_full + 8 * sk, (j / SK) & 1, p.err, abort_flag)) break;
+        // S buffer sb held P_{j-2}: wait until P.V of tile j-2 has consumed it.
+        if (j >= 2 && !mbar_wait_bounded(o_done, (j - 2) & 1, p.err, abort_flag)) break;
+        tc::fence_after_sync();
+        const uint32_t kbase = sK + sk * L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          tc::mma_ss(tmem + L::kColS + 128 * sb, tc::sdesc_sw128(sQ + off, 16, 1024),
+                     tc::sdesc_sw128(kbase + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+        }
+        tc::commit(k_empty + 8 * sk);
+        tc::commit(s_full + 8 * sb);
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && !*abort_flag && issue_pv(n_kv - 1)) tc::commit(o_final);
+      // Every MMA this thread issued has finished once `drain` completes.
+      tc::commit(drain);
+      mbar_wait_bounded(drain, 0, nullptr, nullptr);
+    }
+  } else {
+    // ============================ softmax warps ============================
+    const int row = tid;  // 0..127: query row of the tile and tensor-memory lane
+    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    const int q_idx = m0 + row;
+    // Last key this row may see (inclusive).
+    const int lim = p.causal ? min(kv_len - 1, q_idx + offset) : kv_len - 1;
+    float m_used = -CUDART_INF_F, l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait_bounded(s_full + 8 * sb, (j >> 1) & 1, p.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float s[BN];
+      {
+        uint32_t r[BN / 32][32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + L::kColS + 128 * sb + 32 * c, r[c]);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[c][i]);
+      }
+      const int kv0 = j * BN;
+      if (kv0 + BN - 1 > lim) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) s[i] = (kv0 + i <= lim) ? s[i] : -CUDART_INF_F;
+      }
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+      mx *= p.scale_log2;
+      float factor = 1.f;
+      bool grow = false;
+      if (mx > m_used + kRescaleThreshold) {
+        factor = (m_used == -CUDART_INF_F) ? 1.f : fast_exp2(m_used - mx);
+        grow = m_used != -CUDART_INF_F;
+        m_used = mx;
+        l_sum *= factor;
+      }
+      if (__any_sync(0xffffffffu, grow)) {
+        // O holds P.V of tiles < j: wait for the last of them, then rescale in place.
+        if (!mbar_wait_bounded(o_done, (j - 1) & 1, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::ld32(lane_base + L::kColO + 32 * c, r);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tc::st32(lane_base + L::kColO + 32 * c, r);
+        }
+        tc::wait_st();
+      }
+      const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 64; ++c) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = fast_exp2(fmaf(s[64 * c + 2 * i], p.scale_log2, -msub));
+          const float p1 = fast_exp2(fmaf(s[64 * c + 2 * i + 1], p.scale_log2, -msub));
+          rowsum += p0 + p1;
+          packed[i] = pack2<T>(p0, p1);
+        }
+        tc::st32(lane_base + L::kColS + 128 * sb + 32 * c, packed);
+      }
+      l_sum += rowsum;
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(p_full + 8 * sb);
+    }
+    // ---- epilogue: O / l -> global ----
+    if (ok && n_kv > 0 && mbar_wait_bounded(o_final, 0, p.err, abort_flag)) {
+      tc::fence_after_sync();
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const bool store = q_idx < q_len;
+      const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tc::ld32(lane_base + L::kColO + 32 * c, r);
+        tc::wait_ld();
+        if (store) {
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + 32 * c);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
+                                   __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + base + 32 * c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack2<T>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+              v.y = pack2<T>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+              v.z = pack2<T>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+              v.w = pack2<T>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+              dst[i] = v;
+            }
+          }
+        }
+      }
+    } else if (n_kv == 0 && q_idx < q_len) {
+      // No visible keys (only reachable with invalid causal inputs): zeros.
+      const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
+      for (int d = 0; d < D; ++d) {
+        if (p.out_f32) {
+          reinterpret_cast<float*>(p.out)[base + d] = 0.f;
+        } else {
+          reinterpret_cast<T*>(p.out)[base + d] = from_float<T>(0.f);
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace pre
+
+// =============================================================================
+// Host side
+// =============================================================================
+namespace {
+
+template <typename T, int D>
+int launch_t(const PrefillArgs& a) {
+  using L = pre::Layout<D>;
+  auto kern = pre::prefill_kernel<T, D>;
+  static_assert(L::kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kSmem));
+  if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill)", e);
+  std::string why;
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[3] = {64u, 1u, uint32_t(pre::BM)};
+  {
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.num_heads), uint64_t(a.total_q)};
+    const uint64_t strides[2] = {uint64_t(a.q_sh) * 2, uint64_t(a.q_st) * 2};
+    if (!encode_tiled(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.q, dims, strides, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B, &why))
+      return invalid("prefill q: " + why);
+  }
+  {
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.num_kv_heads), uint64_t(a.total_k)};
+    const uint64_t sk[2] = {uint64_t(a.k_sh) * 2, uint64_t(a.k_st) * 2};
+    const uint64_t sv[2] = {uint64_t(a.v_sh) * 2, uint64_t(a.v_st) * 2};
+    if (!encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.k, dims, sk, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                      &why))
+      return invalid("prefill k: " + why);
+    if (!encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.v, dims, sv, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                      &why))
+      return invalid("prefill v: " + why);
+  }
+  pre::Params p;
+  p.cu_q = a.cu_q;
+  p.cu_k = a.cu_k;
+  p.out = a.out;
+  p.o_st = a.o_st;
+  p.o_sh = a.o_sh;
+  p.num_heads = a.num_heads;
+  p.group = a.num_heads / a.num_kv_heads;
+  p.scale_log2 = float(double(a.softmax_scale) * 1.4426950408889634);
+  p.causal = a.causal ? 1 : 0;
+  p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
+  p.err = a.error_word;
+  const int m_tiles = (a.max_seqlen_q + pre::BM - 1) / pre::BM;
+  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(m_tiles));
+  kern<<<grid, pre::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_failure("prefill launch", e);
+  return FAT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int launch_prefill_varlen(const PrefillArgs& a) {
+  if (a.batch < 0 || a.total_q < 0 || a.total_k < 0) return invalid("prefill_varlen: sizes must be non-negative");
+  if (a.num_heads <= 0 || a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads != 0)
+    return invalid("prefill_varlen: num_heads must be a positive multiple of num_kv_heads");
+  if (a.dtype != FAT_DTYPE_F16 && a.dtype != FAT_DTYPE_BF16)
+    return unsupported("prefill_varlen: q/k/v must be fp16 or bf16");
+  if (a.out_dtype != a.dtype && a.out_dtype != FAT_DTYPE_F32)
+    return invalid("prefill_varlen: out dtype must be the input dtype or fp32");
+  if (a.batch == 0 || a.total_q == 0 || a.max_seqlen_q <= 0) return FAT_OK;
+  if (a.q == nullptr || a.k == nullptr || a.v == nullptr || a.out == nullptr || a.cu_q == nullptr ||
+      a.cu_k == nullptr)
+    return invalid("prefill_varlen: null pointer argument");
+  if (a.total_k == 0) return invalid("prefill_varlen: no keys");
+  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || (a.q_st * 2) % 16 || (a.q_sh * 2) % 16 ||
+      (a.k_st * 2) % 16 || (a.k_sh * 2) % 16 || (a.v_st * 2) % 16 || (a.v_sh * 2) % 16)
+    return unsupported("prefill_varlen: q/k/v must be 16-byte aligned with 16-byte-multiple strides");
+  if (!aligned16(a.out) || (a.o_st * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16 ||
+      (a.o_sh * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16)
+    return unsupported("prefill_varlen: out must be 16-byte aligned with 16-byte-multiple strides");
+  if (a.max_seqlen_q > 65535 * pre::BM) return unsupported("prefill_varlen: max_seqlen_q too large");
+  const bool bf = a.dtype == FAT_DTYPE_BF16;
+  switch (a.head_dim) {
+    case 64:
+      return bf ? launch_t<__nv_bfloat16, 64>(a) : launch_t<__half, 64>(a);
+    case 128:
+      return bf ? launch_t<__nv_bfloat16, 128>(a) : launch_t<__half, 128>(a);
+    default:
+      return unsupported("prefill_varlen: head_dim must be 64 or 128, got " + std::to_string(a.head_dim));
+  }
+}
+
+}  // namespace fat

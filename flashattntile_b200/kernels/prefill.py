@@ -89,9 +89,31 @@ def launch_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen
         if not t.is_cuda:
             raise RuntimeError("flashattntile_b200 runs on CUDA tensors only; it has no CPU path")
     lib = _lib.load()
-    if not hasattr(lib, "fat_prefill_varlen"):
-        raise NotImplementedError("this build of libflashattn_sm100.so has no prefill kernel")
-    raise NotImplementedError("prefill kernel not wired yet")
+    dev = q.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+
+    def aligned(t):
+        eb = t.element_size()
+        ok = (t.stride(2) == 1 and t.data_ptr() % 16 == 0 and (t.stride(0) * eb) % 16 == 0
+              and (t.stride(1) * eb) % 16 == 0)
+        return t if ok else t.contiguous()
+
+    q, k, v = aligned(q), aligned(k), aligned(v)
+    cu_seqlens_q = cu_seqlens_q.contiguous()
+    cu_seqlens_k = cu_seqlens_k.contiguous()
+    out_dtype = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype, device=dev)
+    with torch.cuda.device(idx):
+        err = _lib.error_word(dev)
+        status = lib.fat_prefill_varlen(
+            q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
+            v.stride(0), v.stride(1), out.data_ptr(), out.stride(0), out.stride(1), cu_seqlens_q.data_ptr(),
+            cu_seqlens_k.data_ptr(), cu_seqlens_q.numel() - 1, q.shape[0], k.shape[0], q.shape[1], k.shape[1],
+            q.shape[2], int(max_seqlen_q), int(max_seqlen_k), int(bool(causal)), float(softmax_scale),
+            _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[out_dtype], err.data_ptr(), _lib.stream_handle(dev))
+    _lib.check(status, "prefill_varlen")
+    return out
 
 
 def prefill_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, max_seqlen_k: int,

@@ -99,6 +99,29 @@ int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, cons
                      int32_t* error_word, void* stream);
 
 /*
+ * Packed varlen prefill: for every sequence b (tokens cu_q[b]..cu_q[b+1] of q and
+ * cu_k[b]..cu_k[b+1] of k/v) and query head h,
+ *   out = softmax(scale * q k^T [+ bottom-right causal mask]) v,
+ * with query i seeing key j when j <= i + kv_len - q_len (causal), query head h
+ * reading KV head h / (num_heads / num_kv_heads), P rounded to the input dtype
+ * before P.V and fp32 accumulation.
+ *
+ *   q   [total_q, num_heads, head_dim], k/v [total_k, num_kv_heads, head_dim]   dtype (F16 | BF16)
+ *   out [total_q, num_heads, head_dim]   out_dtype (= dtype, or F32)
+ *   cu_q, cu_k  int32 [batch + 1], non-decreasing from 0 (not checked on the device)
+ *
+ * head_dim in {64, 128}; all bases 16-byte aligned, token/head strides multiples
+ * of 16 bytes.  max_seqlen_q bounds the launch grid (queries past it are not
+ * computed).  Allocates nothing.
+ */
+int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                       int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, void* out,
+                       int64_t out_stride_t, int64_t out_stride_h, const int32_t* cu_seqlens_q,
+                       const int32_t* cu_seqlens_k, int batch, int64_t total_q, int64_t total_k, int num_heads,
+                       int num_kv_heads, int head_dim, int max_seqlen_q, int max_seqlen_k, int causal,
+                       float softmax_scale, int dtype, int out_dtype, int32_t* error_word, void* stream);
+
+/*
  * Page-table gather: out_k/out_v [batch, max_len, num_kv_heads, row_bytes] (contiguous)
  * receive, bit for bit, the rows of each sequence's first seq_lens[b] tokens, and
  * zeros past that.  The cache is addressed by byte strides (page, slot, head); the

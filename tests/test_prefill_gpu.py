@@ -1,0 +1,151 @@
+"""Varlen prefill on the GPU against the oracle and the reference's golden outputs.
+
+Mirrors FlashAttnTile's prefill tests (``tests/test_prefill.py``,
+``tests/test_kernel_correctness.py:71-122``): ragged and odd lengths, head dims
+64/128, GQA / MQA / MHA, causal and not, fp16 / bf16, a query tile longer than
+the sequence, kv_len > q_len bottom-right alignment, and comparison with
+torch SDPA; plus the benchmark's cfg3 shape at full size.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import golden_names, load_golden
+from helpers import TAG, assert_close_f32, assert_parity_16bit, from_np, to_np, varlen_case
+
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ODD_LENS = [1, 17, 255, 1000]
+GQA_CASES = [(8, 8), (8, 2), (8, 1)]
+# P enters P.V rounded to the input dtype, as in the reference kernel
+# (prefill.py:128); the fp32-output comparison bounds that rounding.
+F32_ATOL = {torch.float16: 2e-3, torch.bfloat16: 8e-3}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import flashattntile_b200  # noqa: F401
+
+
+def _run(q, k, v, cu_q, cu_k, causal, out_dtype=None, scale=None):
+    from flashattntile_b200.kernels.prefill import launch_prefill
+
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    qlens = (cu_q[1:] - cu_q[:-1]).tolist()
+    klens = (cu_k[1:] - cu_k[:-1]).tolist()
+    out = launch_prefill(q.to(DEV), k.to(DEV), v.to(DEV), cu_q.to(DEV), cu_k.to(DEV), max(qlens), max(klens),
+                         causal, scale, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle(q, k, v, cu_q, cu_k, causal, dtype, out_f32=False):
+    return oatt.attention_varlen(to_np(q), to_np(k), to_np(v), to_np(cu_q), to_np(cu_k), causal, dtype=TAG[dtype],
+                                 out_f32=out_f32)
+
+
+def _check(q, k, v, cu_q, cu_k, causal, dtype):
+    import flashattntile_b200 as fat
+
+    out = _run(q, k, v, cu_q, cu_k, causal)
+    assert out.dtype == dtype and out.shape == q.shape
+    worst16 = assert_parity_16bit(out, _oracle(q, k, v, cu_q, cu_k, causal, dtype), dtype,
+                                  atol=F32_ATOL[dtype])
+    out32 = _run(q, k, v, cu_q, cu_k, causal, out_dtype=torch.float32)
+    worst32 = assert_close_f32(out32, _oracle(q, k, v, cu_q, cu_k, causal, dtype, out_f32=True),
+                               atol=F32_ATOL[dtype])
+    assert fat.device_error() == 0
+    return worst16, worst32
+
+
+@pytest.mark.parametrize("name", golden_names("prefill_"))
+def test_prefill_matches_reference_golden(name):
+    c = load_golden(name)
+    dtype = {"f16": torch.float16, "bf16": torch.bfloat16}[c["meta"]["dtype"]]
+    q, k, v = (from_np(c[n], dtype) for n in ("q", "k", "v"))
+    cu_q, cu_k = torch.from_numpy(c["cu_q"]), torch.from_numpy(c["cu_k"])
+    causal = c["meta"]["causal"]
+    out = _run(q, k, v, cu_q, cu_k, causal)
+    assert_parity_16bit(out, c["out"], dtype, atol=F32_ATOL[dtype])
+    out32 = _run(q, k, v, cu_q, cu_k, causal, out_dtype=torch.float32)
+    assert_close_f32(out32, c["out_f32"], atol=F32_ATOL[dtype])
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("heads,kv_heads", GQA_CASES)
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_matrix(head_dim, heads, kv_heads, causal, dtype):
+    q, k, v, cu_q, cu_k = varlen_case(7, ODD_LENS, ODD_LENS, heads, kv_heads, head_dim, dtype, scale=0.2)
+    _check(q, k, v, cu_q, cu_k, causal, dtype)
+
+
+@pytest.mark.parametrize("seqlen", ODD_LENS)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_single_odd_length_unit_scale(seqlen, dtype):
+    q, k, v, cu_q, cu_k = varlen_case(8, [seqlen], [seqlen], 8, 2, 128, dtype)
+    for causal in (True, False):
+        _check(q, k, v, cu_q, cu_k, causal, dtype)
+
+
+def test_prefill_kv_longer_than_q_bottom_right():
+    q, k, v, cu_q, cu_k = varlen_case(9, [3, 130, 1, 40], [300, 130, 77, 400], 8, 2, 64, torch.float16)
+    _check(q, k, v, cu_q, cu_k, True, torch.float16)
+    _check(q, k, v, cu_q, cu_k, False, torch.float16)
+
+
+def test_prefill_zero_length_sequences_in_batch():
+    q, k, v, cu_q, cu_k = varlen_case(10, [5, 0, 70, 0], [5, 0, 70, 3], 4, 4, 64, torch.float16)
+    _check(q, k, v, cu_q, cu_k, True, torch.float16)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("heads,kv_heads", GQA_CASES)
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_matches_sdpa(head_dim, heads, kv_heads, causal, dtype):
+    gen = torch.Generator().manual_seed(9)
+    batch, seqlen = 2, 255
+    q = (torch.randn(batch, heads, seqlen, head_dim, generator=gen) * 0.2).to(dtype).to(DEV)
+    k = (torch.randn(batch, kv_heads, seqlen, head_dim, generator=gen) * 0.2).to(dtype).to(DEV)
+    v = (torch.randn(batch, kv_heads, seqlen, head_dim, generator=gen) * 0.2).to(dtype).to(DEV)
+    qt = q.transpose(1, 2).reshape(batch * seqlen, heads, head_dim)
+    kt = k.transpose(1, 2).reshape(batch * seqlen, kv_heads, head_dim)
+    vt = v.transpose(1, 2).reshape(batch * seqlen, kv_heads, head_dim)
+    cu = torch.tensor([b * seqlen for b in range(batch + 1)], dtype=torch.int32)
+    out = _run(qt, kt, vt, cu, cu, causal)
+    out = out.reshape(batch, seqlen, heads, head_dim).transpose(1, 2)
+    g = heads // kv_heads
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.float(), k.repeat_interleave(g, 1).float(), v.repeat_interleave(g, 1).float(), is_causal=causal)
+    torch.testing.assert_close(out.float(), ref, atol=1e-2, rtol=1e-2)
+
+
+def test_prefill_op_and_non_contiguous_views():
+    import flashattntile_b200  # noqa: F401
+
+    q, k, v, cu_q, cu_k = varlen_case(11, [33, 7], [33, 7], 8, 2, 64, torch.float16)
+    qkv = torch.cat([q, k, v], dim=1).to(DEV)  # [T, 8 + 2 + 2, 64] packed projection output
+    qv, kv_, vv = qkv[:, :8], qkv[:, 8:10], qkv[:, 10:12]
+    out = torch.ops.flashattn_tile.prefill_varlen(qv, kv_, vv, cu_q.to(DEV), cu_k.to(DEV), 33, 33, True, 0.125)
+    want = oatt.attention_varlen(to_np(q), to_np(k), to_np(v), to_np(cu_q), to_np(cu_k), True, scale=0.125,
+                                 dtype="f16")
+    assert_parity_16bit(out, want, torch.float16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_cfg3_full_size_parity(dtype):
+    """BASELINE cfg3: lens {512, 1024, 2048, 4096}, H32/8, D128, causal."""
+    lens = [512, 1024, 2048, 4096]
+    q, k, v, cu_q, cu_k = varlen_case(3, lens, lens, 32, 8, 128, dtype)
+    out32 = _run(q, k, v, cu_q, cu_k, True, out_dtype=torch.float32)
+    want = _oracle(q, k, v, cu_q, cu_k, True, dtype, out_f32=True)
+    err = np.abs(out32.cpu().numpy() - want)
+    assert err.max() <= F32_ATOL[dtype], f"max-abs {err.max():.3e}"
+    assert err.mean() <= 2e-4
