@@ -103,10 +103,14 @@ struct Layout {
                                   size_t(kStages) * sizeof(Meta) + size_t(kMergeFloats) * 4 +
                                   size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16 + kRingBytes + 16;
 
-  // Shared address of byte column `bc` (multiple of 16) of token row `row` of a tile.
+  // Shared address of byte column `bc` (16-byte aligned part) of token row `row`
+  // of a tile stored as [row][kCB column blocks][128 B]: with the 128-byte
+  // swizzle, 16-byte chunk c of 128-byte segment g (g = row * kCB + block)
+  // sits at chunk position c ^ (g & 7).
   static __device__ __forceinline__ uint32_t addr(uint32_t tile, int row, int bc) {
     if constexpr (kBoxBytes == 128) {
-      return tile + uint32_t(bc >> 7) * uint32_t(kChunk * 128) + swz128(uint32_t(row), uint32_t((bc & 127) >> 4));
+      const uint32_t seg = uint32_t(row * kCB + (bc >> 7));
+      return tile + seg * 128u + ((uint32_t((bc & 127) >> 4) ^ (seg & 7u)) << 4) + uint32_t(bc & 15);
     } else {
       return tile + uint32_t(row * kBoxBytes + bc);
     }
@@ -308,17 +312,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* rks = reinterpret_cast<float*>(rids + kRing * 8);
     float* rvs = rks + kRing * 8;
     if (x0 < x1) {
+      // Chunk counters relative to x0 fit in 32 bits; the walk keeps
+      // (sequence, unit, chunk) incrementally so the loop does no 64-bit
+      // division (emulated and slow on the GPU).
+      const int n = int(x1 - x0);
       int wb = int(shl[0]);
       long long wS = shl[1];
       int wlen = max(__ldg(p.seq_lens + wb), 0);
       int wchunks = (wlen + kChunk - 1) / kChunk;
-      long long wpos = x0 - wS * nkg;
-      long long xl = x0;
+      int wunit, wchunk;
+      {
+        const long long pos = x0 - wS * nkg;
+        wunit = int(pos / wchunks);
+        wchunk = int(pos - (long long)wunit * wchunks);
+      }
+      int il = 0;  // next chunk (relative to x0) whose ids are fetched
       auto prefetch_ids = [&]() {
-        if (xl < x1) {
-          const int r = int((xl - x0) % kRing);
-          const int unit_local = int(wpos / wchunks);
-          const int chunk = int(wpos - (long long)unit_local * wchunks);
+        if (il < n) {
+          const int r = il & (kRing - 1);
+          const int unit_local = wunit;
+          const int chunk = wchunk;
           const int tok0 = chunk * kChunk;
           const int nbox = (min(kChunk, wlen - tok0) + p.box_rows - 1) / p.box_rows;
           if (lane == 0) {
@@ -339,25 +352,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               *dst = -1;
             }
           }
-          ++xl;
-          ++wpos;
-          if (wpos == (long long)wchunks * nkg && xl < x1) {
-            wS += wchunks;
-            wpos = 0;
-            do {
-              ++wb;
-              wlen = max(__ldg(p.seq_lens + wb), 0);
-              wchunks = (wlen + kChunk - 1) / kChunk;
-            } while (wchunks == 0 && wb + 1 < p.batch);
+          ++il;
+          if (++wchunk == wchunks) {
+            wchunk = 0;
+            if (++wunit == nkg && il < n) {
+              wunit = 0;
+              wS += wchunks;
+              do {
+                ++wb;
+                wlen = max(__ldg(p.seq_lens + wb), 0);
+                wchunks = (wlen + kChunk - 1) / kChunk;
+              } while (wchunks == 0 && wb + 1 < p.batch);
+            }
           }
         }
         cp_async_commit();
       };
-      // Scales of chunk xs (its page ids must have landed): 8-bit caches only.
-      auto prefetch_scales = [&](long long xs) {
+      // Scales of chunk i (its page ids must have landed): 8-bit caches only.
+      auto prefetch_scales = [&](int i) {
         if constexpr (EB == 1) {
-          if (xs >= x0 && xs < x1) {
-            const int r = int((xs - x0) % kRing);
+          if (i >= 0 && i < n) {
+            const int r = i & (kRing - 1);
             const int nbox = rinfo[r].nbox;
             const int kvh = rinfo[r].unit_local / p.head_groups;
             if (lane < nbox) {
@@ -376,25 +391,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       // scales of chunk y we need y's ids: 2*(kPF-kPF2) groups were committed
       // after them.  Before filling the stage of chunk x (step x-x0+kPF) we
       // need x's scales: 2*kPF2 groups were committed after them.
-      auto step = [&](long long k) {
+      auto step = [&](int k) {
         prefetch_ids();
         cp_async_wait<2 * (kPF - kPF2)>();
         __syncwarp();
-        prefetch_scales(x0 + k - (kPF - kPF2));
+        prefetch_scales(k - (kPF - kPF2));
       };
       for (int k = 0; k < kPF; ++k) step(k);
       bool full_seg = false;
-      for (long long x = x0; x < x1; ++x) {
-        step(x - x0 + kPF);
+      for (int i = 0; i < n; ++i) {
+        step(i + kPF);
         cp_async_wait<2 * kPF2>();
         __syncwarp();
-        const int r = int((x - x0) % kRing);
+        const int r = i & (kRing - 1);
         const int b = rinfo[r].b, unit_local = rinfo[r].unit_local, chunk = rinfo[r].chunk;
         const int len = rinfo[r].len, chunks_b = rinfo[r].chunks_b, nbox = rinfo[r].nbox;
         const long long S = rinfo[r].S;
-        const bool first = (x == x0) || chunk == 0;
-        const bool last = (x == x1 - 1) || chunk == chunks_b - 1;
-        if (first) full_seg = (chunk == 0) && (x1 - x >= chunks_b);
+        const bool first = (i == 0) || chunk == 0;
+        const bool last = (i == n - 1) || chunk == chunks_b - 1;
+        if (first) full_seg = (chunk == 0) && (n - i >= chunks_b);
         const int s = it % kStages;
         const uint32_t parity = uint32_t(((it / kStages) & 1) ^ 1);
         if (!mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) break;
@@ -457,20 +472,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t fb = full0 + 8u * s;
         if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
         __syncwarp();
-        const int nops = nbox * L::kCB * 2;
+        // One TMA copy per (row box, K|V): the box spans every 128-byte column
+        // block of its rows (5-D map), landing as [rows][row bytes] in the stage.
         const uint32_t st = smem_u32(stages) + uint32_t(s) * L::kStage;
-        for (int j0 = 0; j0 < nops; j0 += 32) {
-          const int j = j0 + lane;
-          const int box = min(j, nops - 1) / (L::kCB * 2);
-          const int ph = __shfl_sync(0xffffffffu, phys, box);
-          if (j < nops && ph >= 0) {
-            const int rem = j - box * (L::kCB * 2);
-            const int tensor = rem / L::kCB;
-            const int cb = rem - tensor * L::kCB;
+        {
+          const int box = lane >> 1, tensor = lane & 1;
+          const int ph = __shfl_sync(0xffffffffu, phys, box & 7);
+          if (box < nbox && ph >= 0) {
             const int t = tok0 + box * p.box_rows;
-            const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(cb) * uint32_t(kChunk * L::kBoxBytes) +
-                                 uint32_t(box * p.box_rows * L::kBoxBytes);
-            tma_load_4d(dst, tensor ? &tm_v : &tm_k, fb, cb * (L::kBoxBytes / EB), kvh, t % p.page_size, ph);
+            const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(box * p.box_rows * L::kRowBytes);
+            tma_load_5d(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph);
           }
         }
         ++it;
@@ -843,17 +854,25 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kSmem));
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(decode)", e);
 
-  const int box_rows = a.page_size < 16 ? a.page_size : 16;
-  const uint64_t dims[4] = {uint64_t(a.head_dim), uint64_t(a.num_kv_heads), uint64_t(a.page_size),
-                            uint64_t(a.num_pages)};
-  const uint64_t strides[3] = {uint64_t(a.kv_sh) * EB, uint64_t(a.kv_ss) * EB, uint64_t(a.kv_sp) * EB};
-  const uint32_t box[4] = {uint32_t(L::kBoxBytes / EB), 1u, uint32_t(box_rows), 1u};
+  // One TMA box covers gcd(page_size, chunk) token rows -- as tall as possible
+  // (whole pages up to the 64-token chunk) while never crossing a page or a
+  // chunk boundary, so large pages need fewer, taller copies.
+  int box_rows = dec::kChunk;
+  while (a.page_size % box_rows) box_rows >>= 1;
+  // 5-D view of the cache: {elements of a 128-byte column block, column block,
+  // kv head, slot, page}; one box = box_rows slots x every column block of one
+  // head, i.e. whole token rows.
+  const uint64_t dims[5] = {uint64_t(L::kBoxBytes / EB), uint64_t(L::kCB), uint64_t(a.num_kv_heads),
+                            uint64_t(a.page_size), uint64_t(a.num_pages)};
+  const uint64_t strides[4] = {uint64_t(L::kBoxBytes), uint64_t(a.kv_sh) * EB, uint64_t(a.kv_ss) * EB,
+                               uint64_t(a.kv_sp) * EB};
+  const uint32_t box[5] = {uint32_t(L::kBoxBytes / EB), uint32_t(L::kCB), 1u, uint32_t(box_rows), 1u};
   const CUtensorMapDataType dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapSwizzle sw = L::kBoxBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUtensorMap tmk, tmv;
   std::string why;
-  if (!encode_tiled(&tmk, dt, 4, a.k_cache, dims, strides, box, sw, &why)) return invalid("k_cache: " + why);
-  if (!encode_tiled(&tmv, dt, 4, a.v_cache, dims, strides, box, sw, &why)) return invalid("v_cache: " + why);
+  if (!encode_tiled(&tmk, dt, 5, a.k_cache, dims, strides, box, sw, &why)) return invalid("k_cache: " + why);
+  if (!encode_tiled(&tmv, dt, 5, a.v_cache, dims, strides, box, sw, &why)) return invalid("v_cache: " + why);
 
   dec::Params p;
   p.q = a.q;
