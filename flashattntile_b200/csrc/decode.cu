@@ -37,7 +37,8 @@ namespace fat {
 namespace dec {
 
 constexpr int kWarps = 4;                  // consumer warps
-constexpr int kThreads = (kWarps + 1) * 32;  // + one producer warp
+constexpr int kProducers = 2;              // producer warps (take turns by chunk)
+constexpr int kThreads = (kWarps + kProducers) * 32;
 constexpr int kChunk = 16 * kWarps;        // tokens per pipeline stage
 constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
 constexpr int kStageBudget = 160 * 1024;   // shared memory for the stage ring
@@ -101,7 +102,8 @@ struct Layout {
   static constexpr int kMergeFloats = kWarps * kRows * (D + 8) + 2 * kWarps * kRows;
   static constexpr size_t kSmem = 1024 /*align slack*/ + size_t(kStages) * kStage + size_t(kStages) * kQBytes +
                                   size_t(kStages) * sizeof(Meta) + size_t(kMergeFloats) * 4 +
-                                  size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16 + kRingBytes + 16;
+                                  size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16 +
+                                  size_t(kProducers) * kRingBytes + 16;
 
   // Shared address of byte column `bc` (16-byte aligned part) of token row `row`
   // of a tile stored as [row][kCB column blocks][128 B]: with the 128-byte
@@ -295,27 +297,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (warp == kWarps) {
-    // ======================= producer warp =======================
+  if (warp >= kWarps) {
+    // ======================= producer warps =======================
+    // kProducers warps take turns: producer `pid` fills the stages of chunks
+    // pid, pid + kProducers, ... of this CTA's range, so the per-chunk
+    // bookkeeping of one warp overlaps with the others' TMA traffic.
+    const int pid = warp - kWarps;
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
     }
-    // The walk over this CTA's chunks runs kPF chunks ahead of the stage
+    // The walk over this CTA's chunks runs kPF own chunks ahead of the stage
     // being filled: for each future chunk it records the unit info in a small
     // shared ring and starts cp.async copies of its page ids (and, for 8-bit
     // caches, kPF2 chunks ahead, of the pages' scales), so the TMA issue for
     // a stage never waits on a dependent global load.
-    int it = 0;
-    RingInfo* rinfo = reinterpret_cast<RingInfo*>(ring_base);
+    const int n = int(x1 - x0);  // chunks of this CTA (fits in 32 bits)
+    const int n_own = n > pid ? (n - pid + kProducers - 1) / kProducers : 0;
+    int own_issued = 0;
+    RingInfo* rinfo = reinterpret_cast<RingInfo*>(ring_base + pid * kRingBytes);
     int* rids = reinterpret_cast<int*>(rinfo + kRing);
     float* rks = reinterpret_cast<float*>(rids + kRing * 8);
     float* rvs = rks + kRing * 8;
-    if (x0 < x1) {
-      // Chunk counters relative to x0 fit in 32 bits; the walk keeps
-      // (sequence, unit, chunk) incrementally so the loop does no 64-bit
-      // division (emulated and slow on the GPU).
-      const int n = int(x1 - x0);
+    if (n_own > 0) {
+      // The walk keeps (sequence, unit, chunk) incrementally, so the loop does
+      // no 64-bit division (emulated and slow on the GPU).
       int wb = int(shl[0]);
       long long wS = shl[1];
       int wlen = max(__ldg(p.seq_lens + wb), 0);
@@ -326,10 +332,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         wunit = int(pos / wchunks);
         wchunk = int(pos - (long long)wunit * wchunks);
       }
-      int il = 0;  // next chunk (relative to x0) whose ids are fetched
+      int wi = 0;  // chunk (relative to x0) the walk points at
+      auto advance = [&]() {
+        ++wi;
+        if (++wchunk == wchunks) {
+          wchunk = 0;
+          if (++wunit == nkg && wi < n) {
+            wunit = 0;
+            wS += wchunks;
+            do {
+              ++wb;
+              wlen = max(__ldg(p.seq_lens + wb), 0);
+              wchunks = (wlen + kChunk - 1) / kChunk;
+            } while (wchunks == 0 && wb + 1 < p.batch);
+          }
+        }
+      };
+      for (int k = 0; k < pid && wi < n; ++k) advance();
+      int jl = 0;  // next own chunk whose ids are fetched
       auto prefetch_ids = [&]() {
-        if (il < n) {
-          const int r = il & (kRing - 1);
+        if (jl < n_own) {
+          const int r = jl & (kRing - 1);
           const int unit_local = wunit;
           const int chunk = wchunk;
           const int tok0 = chunk * kChunk;
@@ -352,27 +375,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               *dst = -1;
             }
           }
-          ++il;
-          if (++wchunk == wchunks) {
-            wchunk = 0;
-            if (++wunit == nkg && il < n) {
-              wunit = 0;
-              wS += wchunks;
-              do {
-                ++wb;
-                wlen = max(__ldg(p.seq_lens + wb), 0);
-                wchunks = (wlen + kChunk - 1) / kChunk;
-              } while (wchunks == 0 && wb + 1 < p.batch);
-            }
-          }
+          ++jl;
+          for (int k = 0; k < kProducers && wi < n; ++k) advance();
         }
         cp_async_commit();
       };
-      // Scales of chunk i (its page ids must have landed): 8-bit caches only.
-      auto prefetch_scales = [&](int i) {
+      // Scales of own chunk j (its page ids must have landed): 8-bit caches only.
+      auto prefetch_scales = [&](int j) {
         if constexpr (EB == 1) {
-          if (i >= 0 && i < n) {
-            const int r = i & (kRing - 1);
+          if (j >= 0 && j < n_own) {
+            const int r = j & (kRing - 1);
             const int nbox = rinfo[r].nbox;
             const int kvh = rinfo[r].unit_local / p.head_groups;
             if (lane < nbox) {
@@ -386,11 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         cp_async_commit();
       };
-      // Step k commits two groups: page ids of chunk x0+k, then scales of
-      // chunk x0+k-(kPF-kPF2) (empty for 16-bit caches).  Before issuing the
+      // Step k commits two groups: page ids of own chunk k, then scales of own
+      // chunk k-(kPF-kPF2) (empty for 16-bit caches).  Before issuing the
       // scales of chunk y we need y's ids: 2*(kPF-kPF2) groups were committed
-      // after them.  Before filling the stage of chunk x (step x-x0+kPF) we
-      // need x's scales: 2*kPF2 groups were committed after them.
+      // after them.  Before filling the stage of own chunk j (step j+kPF) we
+      // need j's scales: 2*kPF2 groups were committed after them.
       auto step = [&](int k) {
         prefetch_ids();
         cp_async_wait<2 * (kPF - kPF2)>();
@@ -398,20 +410,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_scales(k - (kPF - kPF2));
       };
       for (int k = 0; k < kPF; ++k) step(k);
-      bool full_seg = false;
-      for (int i = 0; i < n; ++i) {
-        step(i + kPF);
+      for (int j = 0; j < n_own; ++j) {
+        const int i = pid + j * kProducers;  // chunk index within the CTA's range
+        step(j + kPF);
         cp_async_wait<2 * kPF2>();
         __syncwarp();
-        const int r = i & (kRing - 1);
+        const int r = j & (kRing - 1);
         const int b = rinfo[r].b, unit_local = rinfo[r].unit_local, chunk = rinfo[r].chunk;
         const int len = rinfo[r].len, chunks_b = rinfo[r].chunks_b, nbox = rinfo[r].nbox;
         const long long S = rinfo[r].S;
         const bool first = (i == 0) || chunk == 0;
         const bool last = (i == n - 1) || chunk == chunks_b - 1;
-        if (first) full_seg = (chunk == 0) && (n - i >= chunks_b);
-        const int s = it % kStages;
-        const uint32_t parity = uint32_t(((it / kStages) & 1) ^ 1);
+        // The CTA covers the whole unit iff its first and last chunks are in range.
+        const bool full_seg = (i - chunk >= 0) && (i - chunk + chunks_b <= n);
+        const int s = i % kStages;
+        const uint32_t parity = uint32_t(((i / kStages) & 1) ^ 1);
         if (!mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) break;
 
         const int kvh = unit_local / p.head_groups;
@@ -484,14 +497,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_5d(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph);
           }
         }
-        ++it;
+        ++own_issued;
       }
     }
     cp_async_wait<0>();
-    // Termination marker (or, after an abort, drain this CTA's own copies).
-    if (!*abort_flag) {
-      const int s = it % kStages;
-      const uint32_t parity = uint32_t(((it / kStages) & 1) ^ 1);
+    // Termination marker, written by the producer that owns slot n (or, after
+    // an abort, drain this producer's own copies).
+    if (!*abort_flag && n % kProducers == pid) {
+      const int s = n % kStages;
+      const uint32_t parity = uint32_t(((n / kStages) & 1) ^ 1);
       if (mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) {
         if (lane == 0) {
           meta[s].flags = kDone;
@@ -500,8 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (*abort_flag && lane == 0) {
-      for (int k = max(0, it - kStages); k < it; ++k) {
-        mbar_wait_bounded(full0 + 8u * (k % kStages), uint32_t((k / kStages) & 1), nullptr, nullptr);
+      for (int j = max(0, own_issued - kStages); j < own_issued; ++j) {
+        const int i = pid + j * kProducers;
+        mbar_wait_bounded(full0 + 8u * (i % kStages), uint32_t((i / kStages) & 1), nullptr, nullptr);
       }
     }
     return;
