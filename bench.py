@@ -7,9 +7,10 @@ N(0,1) K/V/Q, block table a seeded permutation of a 32x256-page pool.
 metric = decode HBM GB/s = algorithmic bytes (Q + K + V + O, FlashAttnTile's
 ``bytes_attention("decode")``) / device time.
 
-* ``value``: K timed launches with inputs resident in HBM (537 MB per step,
-  4x the 126 MB L2; L2 is also flushed between steps), CUDA events per step
-  on the launching stream, max over ranks.
+* ``value``: K launches run back to back with inputs resident in HBM (537 MB
+  per step, 4x the 126 MB L2, so no step finds its inputs in L2 and no flush
+  is needed), CUDA events around each step on the launching stream, max over
+  ranks.
 * ``e2e``: the same step through the public op ``torch.ops.flashattn_tile.paged_decode``
   as a serving step calls it -- the per-step inputs (q, page table, seq_lens)
   copied from pinned host memory, the default host-side validation, the output
@@ -47,7 +48,6 @@ if str(ROOT) not in sys.path:
 import torch  # noqa: E402
 
 CFG2 = dict(batch=32, heads=32, kv_heads=8, head_dim=128, page_size=16, ctx=4096)
-FLUSH_BYTES = 256 << 20  # > 126 MB L2
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at cfg2 from the
 # committed ncu capture (profiles/decode_sm100_cfg2.md); None until captured.
 NCU_TRAFFIC_BYTES = {"decode_cfg2": None}
@@ -228,7 +228,6 @@ def main() -> None:
     nbytes = decode_bytes(lens_list, c["heads"], c["kv_heads"], c["head_dim"], c["page_size"])
     scale = c["head_dim"] ** -0.5
     out = torch.empty_like(q)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
 
     def step():
         launch_decode(q, k, v, table, lens, c["page_size"], scale, 1, out=out)
@@ -237,7 +236,7 @@ def main() -> None:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clocks:
-        times = time_steps(step, args.steps, args.warmup, flush)
+        times = time_steps(step, args.steps, args.warmup, None)
     torch.cuda.synchronize()
     total_ms = sum(times)
     if dist is not None:
@@ -265,7 +264,7 @@ def main() -> None:
         o = torch.ops.flashattn_tile.paged_decode(q_d, k, v, t_d, l_d, c["page_size"], scale, 1)
         o_h.copy_(o, non_blocking=True)
 
-    e2e_times = time_steps(e2e_step, max(10, args.steps // 2), args.warmup, flush)
+    e2e_times = time_steps(e2e_step, max(10, args.steps // 2), args.warmup, None)
     e2e_ms = sum(e2e_times) / len(e2e_times)
     if dist is not None:
         t = torch.tensor([e2e_ms], device=device)
@@ -305,7 +304,7 @@ def main() -> None:
             "config": {"workload": "cfg2 paged decode", "batch_per_gpu": c["batch"], "global_batch": c["batch"] * world,
                        "ctx": c["ctx"], "heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
                        "page_size": c["page_size"], "parallelism": f"shard (sequence, kv-head) x{world}, no comm",
-                       "l2": "inputs 537 MB > 126 MB L2, and 256 MB L2 flush between steps"},
+                       "l2": "inputs 537 MB per step > 126 MB L2; steps back to back, no flush"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"] + " copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
@@ -371,6 +370,39 @@ def run_secondary(device, args, peaks) -> dict:
         res[f"cfg4_decode_{mode}"] = {"value": round(gbs, 1), "unit": "GB/s", "ms": round(ms, 4),
                                       "algorithmic_bytes": nbytes, "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)}
         del kq, vq, ks, vs
+    torch.cuda.empty_cache()
+
+    # cfg3: varlen causal prefill, lens {512, 1024, 2048, 4096}, H32/8, D128, fp16 and bf16.
+    from flashattntile_b200.autotune import flops_attention_varlen
+    from flashattntile_b200.kernels.prefill import launch_prefill
+
+    lens = [512, 1024, 2048, 4096]
+    flops = flops_attention_varlen(32, 128, lens, lens, causal=True)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device=device)
+    g3 = torch.Generator(device=device).manual_seed(2)
+    for dt in (torch.float16, torch.bfloat16):
+        # Two input sets used alternately: 2 x 157 MB > L2, so no step reuses L2-resident inputs.
+        sets = []
+        for _ in range(2):
+            q3 = torch.randn((sum(lens), 32, 128), generator=g3, device=device).to(dt)
+            k3 = torch.randn((sum(lens), 8, 128), generator=g3, device=device).to(dt)
+            v3 = torch.randn((sum(lens), 8, 128), generator=g3, device=device).to(dt)
+            sets.append((q3, k3, v3, torch.empty_like(q3)))
+        state = {"i": 0}
+
+        def pstep():
+            q3, k3, v3, o3 = sets[state["i"] & 1]
+            state["i"] += 1
+            launch_prefill(q3, k3, v3, cu, cu, 4096, 4096, True, 128 ** -0.5, out=o3)
+
+        times = time_steps(pstep, max(10, args.steps // 2), args.warmup, None)
+        ms = statistics.mean(times)
+        tflops = flops / (ms * 1e-3) / 1e12
+        res[f"cfg3_prefill_{'f16' if dt == torch.float16 else 'bf16'}"] = {
+            "value": round(tflops, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "algorithmic_flops": flops,
+            "frac_tensor": round(tflops / peaks["bf16_tflops"], 4),
+            "peak_source": "measured cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops)"}
+        del sets
     torch.cuda.empty_cache()
     return res
 

@@ -133,26 +133,39 @@ _WS: dict[tuple[int, int], torch.Tensor] = {}
 _ERR: dict[tuple[int, int], torch.Tensor] = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
-    buf = _WS.get(key)
+def workspace_for(index: int, stream: int, device: torch.device, nbytes: int) -> torch.Tensor:
+    buf = _WS.get((index, stream))
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
-        _WS[key] = buf
+        _WS[(index, stream)] = buf
     return buf
+
+
+def error_word_for(index: int, stream: int, device: torch.device) -> torch.Tensor:
+    buf = _ERR.get((index, stream))
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[(index, stream)] = buf
+    return buf
+
+
+def _key(device: torch.device) -> tuple[int, int]:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return index, torch.cuda.current_stream(torch.device("cuda", index)).cuda_stream
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    index, stream = _key(device)
+    return workspace_for(index, stream, device, nbytes)
 
 
 def error_word(device: torch.device) -> torch.Tensor:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
-    buf = _ERR.get(key)
-    if buf is None:
-        buf = torch.zeros(1, dtype=torch.int32, device=device)
-        _ERR[key] = buf
-    return buf
+    index, stream = _key(device)
+    return error_word_for(index, stream, device)
 
 
 def reset_workspace(device: torch.device) -> None:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
+    key = _key(device)
     if key in _WS:
         _WS[key].zero_()
     if key in _ERR:

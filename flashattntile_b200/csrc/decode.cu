@@ -866,7 +866,7 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   using L = dec::Layout<D, EB>;
   auto kern = dec::paged_decode_kernel<T, D, KVT>;
   static_assert(L::kSmem <= 227 * 1024, "decode stage ring exceeds shared memory");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kSmem));
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(decode)", e);
 
   // One TMA box covers gcd(page_size, chunk) token rows -- as tall as possible

@@ -1,6 +1,8 @@
 #include "host_util.h"
 
 #include <mutex>
+#include <set>
+#include <utility>
 #include <vector>
 
 #include "../../include/flashattn_tile_b200.h"
@@ -51,6 +53,17 @@ int current_device() {
   int dev = 0;
   cudaGetDevice(&dev);
   return dev;
+}
+
+cudaError_t ensure_smem_limit(const void* func, int bytes, int device) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(func, device);
+  if (done.count(key)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
 }
 
 int sm_count(int device) {

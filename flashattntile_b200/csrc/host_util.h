@@ -25,6 +25,9 @@ int sm_count(int device);
 // Current device of the calling thread.
 int current_device();
 
+// Raise `func`'s dynamic shared-memory limit to `bytes` once per (kernel, device).
+cudaError_t ensure_smem_limit(const void* func, int bytes, int device);
+
 // cuTensorMapEncodeTiled resolved through cudaGetDriverEntryPoint.
 // dims/strides are innermost-first; strides[i] is the byte stride of dim i+1.
 bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,

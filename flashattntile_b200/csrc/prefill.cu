@@ -362,7 +362,7 @@ int launch_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
   auto kern = pre::prefill_kernel<T, D>;
   static_assert(L::kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kSmem));
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill)", e);
   std::string why;
   CUtensorMap tq, tk, tv;

@@ -60,10 +60,7 @@ def _validate_decode_inputs(q: torch.Tensor, cache: PagedKVCache) -> None:
     """``decode.py:503-522``: same checks, exception types and messages."""
     if not isinstance(cache, PagedKVCache):
         raise TypeError("cache must be a PagedKVCache")
-    if _config.validate_values():
-        validate_cache(cache)
-    else:
-        validate_metadata(cache)
+    stats = validate_cache(cache) if _config.validate_values() else validate_metadata(cache)
     if q.dim() != 3:
         raise ValueError(f"q must be [batch, heads, head_dim], got {tuple(q.shape)}")
     if q.shape[0] != cache.batch_size:
@@ -76,7 +73,7 @@ def _validate_decode_inputs(q: torch.Tensor, cache: PagedKVCache) -> None:
         raise ValueError("q and cache must live on the same device")
     if not q.is_floating_point():
         raise ValueError(f"q must be floating point, got {q.dtype}")
-    if _config.validate_values() and cache.batch_size and int(cache.seq_lens.min()) <= 0:
+    if stats is not None and stats[0] <= 0:
         raise ValueError("decode requires every sequence to hold at least one cached token")
 
 
@@ -125,18 +122,20 @@ def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_
         if k_scale.stride(1) != 1 or v_scale.stride() != k_scale.stride():
             k_scale, v_scale = k_scale.contiguous(), v_scale.contiguous()
         scale_stride = k_scale.stride(0)
-    with torch.cuda.device(idx):
-        ws_bytes = lib.fat_paged_decode_workspace_size(idx, batch, heads, kvh, dim)
-        ws = _lib.workspace(dev, ws_bytes)
-        err = _lib.error_word(dev)
-        status = lib.fat_paged_decode(
-            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws = _lib.workspace_for(idx, stream, dev, lib.fat_paged_decode_workspace_size(idx, batch, heads, kvh, dim))
+    err = _lib.error_word_for(idx, stream, dev)
+    args = (q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
             k_cache.stride(1), k_cache.stride(2), k_cache.shape[0], page_table.data_ptr(), page_table.stride(0),
             page_table.shape[1], seq_lens.data_ptr(), _lib.ptr(k_scale), _lib.ptr(v_scale), scale_stride,
             out.data_ptr(), out.stride(0), out.stride(1), batch, heads, kvh, dim, int(page_size),
             _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[k_cache.dtype], _lib.DTYPE_CODE[out_dtype],
-            float(softmax_scale), int(split_k), ws.data_ptr(), ws.numel(), err.data_ptr(),
-            _lib.stream_handle(dev))
+            float(softmax_scale), int(split_k), ws.data_ptr(), ws.numel(), err.data_ptr(), stream)
+    if idx == torch.cuda.current_device():
+        status = lib.fat_paged_decode(*args)
+    else:
+        with torch.cuda.device(idx):
+            status = lib.fat_paged_decode(*args)
     _lib.check(status, "paged_decode")
     return out
 

@@ -87,22 +87,41 @@ def validate_metadata(cache: PagedKVCache) -> None:
     _assert(cache.page_table.device == cache.seq_lens.device, "page_table and seq_lens must live on the same device")
 
 
-def validate_cache(cache: PagedKVCache, *, check_pages: bool = True) -> None:
+def cache_value_stats(cache: PagedKVCache) -> tuple[int, int, int, int]:
+    """``(min seq_len, max seq_len, min used page id, max used page id)`` in one
+    device->host transfer.  "Used" entries are those a sequence's length reaches
+    (the first ``ceil(max_len / page_size)`` columns, as the reference checks);
+    with no used entry the page bounds are reported as ``(0, -1)``."""
+    lens = cache.seq_lens
+    table = cache.page_table
+    need = torch.div(lens.max().to(torch.int64) + cache.page_size - 1, cache.page_size, rounding_mode="floor")
+    cols = torch.arange(table.shape[1], device=table.device)
+    used = (cols < need.to(table.device))[None, :].expand_as(table)
+    big = torch.iinfo(torch.int32).max
+    pmin = torch.where(used, table, torch.full_like(table, big)).amin()
+    pmax = torch.where(used, table, torch.full_like(table, -1)).amax()
+    lo, hi = torch.aminmax(lens)
+    stats = torch.stack([lo.to(torch.int64), hi.to(torch.int64), pmin.to(torch.int64).to(lo.device),
+                         pmax.to(torch.int64).to(lo.device)]).tolist()
+    if stats[2] == big:
+        stats[2], stats[3] = 0, -1
+    return int(stats[0]), int(stats[1]), int(stats[2]), int(stats[3])
+
+
+def validate_cache(cache: PagedKVCache, *, check_pages: bool = True) -> tuple[int, int] | None:
     """All checks of ``flashattn_tile/paging.py:84-130``, including the value
-    checks that read ``seq_lens`` / ``page_table`` back to the host."""
+    checks on ``seq_lens`` / ``page_table`` -- read back in a single device->host
+    transfer.  Returns ``(min seq_len, max seq_len)`` (None for an empty batch)."""
     validate_metadata(cache)
     if cache.seq_lens.numel() == 0:
-        return
-    lo, hi = torch.aminmax(cache.seq_lens)
-    _assert(int(lo) >= 0, "seq_lens must be non-negative")
-    max_len = int(hi)
+        return None
+    lo, max_len, umin, umax = cache_value_stats(cache)
+    _assert(lo >= 0, "seq_lens must be non-negative")
     _assert(max_len <= cache.capacity, f"seq_len {max_len} exceeds page-table capacity {cache.capacity}")
     if check_pages and max_len > 0:
-        used = cache.page_table[:, : math.ceil(max_len / cache.page_size)]
-        umin, umax = torch.aminmax(used)
-        _assert(int(umin) >= 0, "page_table contains a negative page id")
-        _assert(int(umax) < cache.num_pages,
-                f"page_table references page {int(umax)} but cache has {cache.num_pages} pages")
+        _assert(umin >= 0, "page_table contains a negative page id")
+        _assert(umax < cache.num_pages, f"page_table references page {umax} but cache has {cache.num_pages} pages")
+    return lo, max_len
 
 
 def allocate(batch: int, max_seq_len: int, num_kv_heads: int, head_dim: int, page_size: int,
