@@ -1,0 +1,78 @@
+"""The C-ABI library: it loads without a GPU and exports every symbol the header declares.
+
+No test here launches device work: the calls below fail host-side validation
+before any CUDA call is made.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def _declared_functions() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(fat_\w+)\s*\(", text))
+    return names
+
+
+def test_library_builds_and_loads():
+    from flashattntile_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.fat_version().decode().startswith("flashattn_tile_b200")
+    assert lib.fat_last_error() is not None
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    from flashattntile_b200 import _lib
+
+    declared = _declared_functions()
+    assert {"fat_paged_decode", "fat_prefill_varlen", "fat_gather_paged"} <= declared
+    raw = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in sorted(declared):
+        assert hasattr(raw, name), f"{name} declared in include/ but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature in _lib.py"
+
+
+def test_host_side_validation_errors_without_gpu():
+    from flashattntile_b200 import _lib
+
+    lib = _lib.load()
+    # num_heads not divisible by num_kv_heads: rejected before any CUDA call.
+    rc = lib.fat_paged_decode(None, 0, 0, None, None, 0, 0, 0, 1, None, 0, 1, None, None, None, 0, None, 0, 0,
+                              2, 3, 2, 128, 16, 0, 0, 0, 0.1, 1, None, 0, None, None)
+    assert rc == _lib.FAT_ERR_INVALID_ARGUMENT
+    assert b"divisible" in lib.fat_last_error()
+    # split_k hint outside 1..64
+    rc = lib.fat_paged_decode(None, 0, 0, None, None, 0, 0, 0, 1, None, 0, 1, None, None, None, 0, None, 0, 0,
+                              2, 4, 2, 128, 16, 0, 0, 0, 0.1, 0, None, 0, None, None)
+    assert rc == _lib.FAT_ERR_INVALID_ARGUMENT and b"split_k" in lib.fat_last_error()
+    # unsupported page size / dtype
+    rc = lib.fat_paged_decode(None, 0, 0, None, None, 0, 0, 0, 1, None, 0, 1, None, None, None, 0, None, 0, 0,
+                              2, 4, 2, 128, 24, 0, 0, 0, 0.1, 1, None, 0, None, None)
+    assert rc == _lib.FAT_ERR_UNSUPPORTED and b"page_size" in lib.fat_last_error()
+    rc = lib.fat_prefill_varlen(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, None, None, 1, 1, 1, 4, 2, 64, 1, 1,
+                                1, 0.1, 2, 2, None, None)
+    assert rc == _lib.FAT_ERR_UNSUPPORTED and b"fp16 or bf16" in lib.fat_last_error()
+
+
+def test_status_codes_map_to_python_exceptions():
+    from flashattntile_b200 import _lib
+
+    _lib.load()
+    with pytest.raises(ValueError):
+        _lib.check(_lib.FAT_ERR_INVALID_ARGUMENT, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.FAT_ERR_UNSUPPORTED, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.FAT_ERR_CUDA, "x")
+    _lib.check(_lib.FAT_OK, "x")
