@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,
          _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp],
     ),
+    "fat_paged_decode_noalloc": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,
+         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _vp],
+    ),
     "fat_prefill_varlen": (
         _i32,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _i32, _i32,
@@ -84,7 +89,11 @@ def load() -> ctypes.CDLL:
                 raise RuntimeError(_ERROR)
             lib = ctypes.CDLL(os.fspath(LIB_PATH))
             for name, (res, args) in SIGNATURES.items():
-                fn = getattr(lib, name)
+                try:
+                    fn = getattr(lib, name)
+                except AttributeError:
+                    _ERROR = f"{LIB_PATH.name} lacks {name}: it is out of date, rebuild it"
+                    raise RuntimeError(_ERROR) from None
                 fn.restype = res
                 fn.argtypes = args
             _LIB = lib

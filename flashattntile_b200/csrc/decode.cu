@@ -950,6 +950,17 @@ size_t decode_workspace_bytes(int device, int batch, int num_heads, int num_kv_h
   return ws_layout(sm_count(device), units, head_dim).total;
 }
 
+void decode_ticket_range(int device, int batch, int num_heads, int num_kv_heads, int head_dim, size_t* offset,
+                         size_t* bytes) {
+  *offset = 0;
+  *bytes = 0;
+  if (num_kv_heads <= 0 || num_heads <= 0 || batch < 0 || head_dim <= 0) return;
+  const int group = num_heads / num_kv_heads;
+  const long long units = (long long)batch * num_kv_heads * ((group + dec::kRows - 1) / dec::kRows);
+  *offset = ws_layout(sm_count(device), units, head_dim).count_off;
+  *bytes = size_t(units) * sizeof(int);
+}
+
 int launch_paged_decode(const DecodeArgs& a) {
   if (a.batch < 0) return invalid("paged_decode: batch must be non-negative");
   if (a.num_heads <= 0 || a.num_kv_heads <= 0) return invalid("paged_decode: head counts must be positive");

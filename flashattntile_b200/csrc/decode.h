@@ -34,6 +34,11 @@ struct DecodeArgs {
 // Scratch bytes for one decode problem: per-CTA split partials + one ticket per unit.
 size_t decode_workspace_bytes(int device, int batch, int num_heads, int num_kv_heads, int head_dim);
 
+// Where, inside that scratch, the per-unit tickets live (they must be zero when a
+// call starts; every successful call leaves them zero).
+void decode_ticket_range(int device, int batch, int num_heads, int num_kv_heads, int head_dim, size_t* offset,
+                         size_t* bytes);
+
 // Validate, build the TMA descriptors and launch. Returns a fat_status.
 int launch_paged_decode(const DecodeArgs& a);
 

@@ -99,6 +99,32 @@ int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, cons
                      int32_t* error_word, void* stream);
 
 /*
+ * fat_paged_decode for callers that cannot allocate device memory.  No
+ * counterpart exists in the reference: it is an addition for engines that
+ * allocate every device buffer up front and forbid allocation afterwards,
+ * plugins whose host framework gives them neither an allocator nor a scratch
+ * pointer, and latency-critical loops where an allocation could synchronise
+ * the device.  Same arguments and result as fat_paged_decode, minus the
+ * workspace: the split scratch is a fixed 4 MiB array in this library's
+ * device memory, held by every GPU that loads the library until the process
+ * exits.  Problems whose scratch would exceed 4 MiB (about
+ * fat_paged_decode_workspace_size) are refused with FAT_ERR_WORKSPACE.  The
+ * first call on a device looks up the array's device address (once per
+ * device; make that first call before any stream capture).  Each call clears
+ * the tickets it uses on `stream`; all calls share the array, so calls that
+ * overlap on the GPU race and must be ordered by the caller.  Allocates
+ * nothing (no cudaMalloc / cudaFree).
+ */
+int fat_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
+                             const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot,
+                             int64_t kv_stride_head, int64_t num_pages, const int32_t* page_table,
+                             int64_t page_table_stride, int64_t max_pages, const int32_t* seq_lens,
+                             const float* k_scale, const float* v_scale, int64_t scale_stride_page, void* out,
+                             int64_t out_stride_b, int64_t out_stride_h, int batch, int num_heads, int num_kv_heads,
+                             int head_dim, int page_size, int q_dtype, int kv_dtype, int out_dtype,
+                             float softmax_scale, int split_k_hint, int32_t* error_word, void* stream);
+
+/*
  * Packed varlen prefill: for every sequence b (tokens cu_q[b]..cu_q[b+1] of q and
  * cu_k[b]..cu_k[b+1] of k/v) and query head h,
  *   out = softmax(scale * q k^T [+ bottom-right causal mask]) v,
