@@ -196,6 +196,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--only", choices=["decode", "quant", "prefill"], default=None,
+                    help="run one workload (profiling); decode = the headline line without secondary")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -222,6 +224,16 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     peaks = _peaks()
+    if args.only in ("quant", "prefill"):
+        res = run_secondary(device, args, peaks, which=(args.only,))
+        if rank == 0:
+            print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup, "results": res}),
+                  flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    if args.only == "decode":
+        args.no_secondary = True
     c = CFG2
     q, k, v, table, lens = make_decode_cfg2(device, seed=1 + rank)
     lens_list = [c["ctx"]] * c["batch"]
@@ -325,8 +337,18 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def run_secondary(device, args, peaks) -> dict:
-    """Quantised decode (cfg4) and, when built, varlen prefill (cfg3)."""
+def run_secondary(device, args, peaks, which=("quant", "prefill")) -> dict:
+    """Quantised decode (cfg4) and varlen prefill (cfg3)."""
+    res = {}
+    if "quant" in which:
+        res.update(run_quant(device, args, peaks))
+    if "prefill" in which:
+        res.update(run_prefill(device, args, peaks))
+    return res
+
+
+def run_quant(device, args, peaks) -> dict:
+    """cfg4: B128, H32/8, D128, ps32, ctx U[1024, 16384], INT8 and e4m3 caches."""
     from flashattntile_b200 import quant
     from flashattntile_b200.kernels.decode import launch_decode
 
@@ -371,11 +393,15 @@ def run_secondary(device, args, peaks) -> dict:
                                       "algorithmic_bytes": nbytes, "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)}
         del kq, vq, ks, vs
     torch.cuda.empty_cache()
+    return res
 
-    # cfg3: varlen causal prefill, lens {512, 1024, 2048, 4096}, H32/8, D128, fp16 and bf16.
+
+def run_prefill(device, args, peaks) -> dict:
+    """cfg3: varlen causal prefill, lens {512, 1024, 2048, 4096}, H32/8, D128, fp16 and bf16."""
     from flashattntile_b200.autotune import flops_attention_varlen
     from flashattntile_b200.kernels.prefill import launch_prefill
 
+    res = {}
     lens = [512, 1024, 2048, 4096]
     flops = flops_attention_varlen(32, 128, lens, lens, causal=True)
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device=device)
