@@ -49,8 +49,8 @@ import torch  # noqa: E402
 
 CFG2 = dict(batch=32, heads=32, kv_heads=8, head_dim=128, page_size=16, ctx=4096)
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at cfg2 from the
-# committed ncu capture (profiles/decode_sm100_cfg2.md); None until captured.
-NCU_TRAFFIC_BYTES = {"decode_cfg2": None}
+# committed ncu capture (profiles/decode_sm100_cfg2.md: 537.72 MB read + 4.23 MB written).
+NCU_TRAFFIC_BYTES = {"decode_cfg2": 541949696}
 
 
 def _peaks() -> dict:
