@@ -11,10 +11,12 @@
 //   A unit split across CTAs is merged by a log-sum-exp combine done by the
 //   last CTA that finishes a piece of it (an atomic ticket per unit); the
 //   math is decode.py:12-14 / 341-352 in base 2.
-// * One producer warp walks the CTA's chunks, reads the page table and issues
-//   TMA tile loads of each page slice ([rows, head_dim] of one KV head, 128-byte
-//   swizzled) into a ring of shared-memory stages guarded by mbarriers.  Each K/V
-//   page is read from HBM once per GQA group, not once per query head.
+// * Two producer warps take turns by chunk: each walks the CTA's chunks,
+//   prefetches page ids (and 8-bit scales) through a cp.async ring, and issues
+//   one 5-D TMA copy per (row box, K|V) -- whole token rows of one KV head,
+//   128-byte swizzled -- into a ring of shared-memory stages guarded by
+//   mbarriers.  Each K/V byte is read from HBM once per GQA group, not once per
+//   query head.
 // * Four consumer warps take 16 tokens each per stage.  Scores and P.V run on
 //   the tensor cores (mma.sync m16n8k16, fp32 accumulate) with the group's
 //   query heads as the M rows; P enters the P.V product as a 16-bit head plus
@@ -884,10 +886,14 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   const uint32_t box[5] = {uint32_t(L::kBoxBytes / EB), uint32_t(L::kCB), 1u, uint32_t(box_rows), 1u};
   const CUtensorMapDataType dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapSwizzle sw = L::kBoxBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  // A token row narrower than 256 B sits next to another head's row: widen L2
+  // fills only to the row itself so that neighbour is not read along with it.
+  const CUtensorMapL2promotion promo =
+      L::kRowBytes >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
   CUtensorMap tmk, tmv;
   std::string why;
-  if (!encode_tiled(&tmk, dt, 5, a.k_cache, dims, strides, box, sw, &why)) return invalid("k_cache: " + why);
-  if (!encode_tiled(&tmv, dt, 5, a.v_cache, dims, strides, box, sw, &why)) return invalid("v_cache: " + why);
+  if (!encode_tiled(&tmk, dt, 5, a.k_cache, dims, strides, box, sw, &why, promo)) return invalid("k_cache: " + why);
+  if (!encode_tiled(&tmv, dt, 5, a.v_cache, dims, strides, box, sw, &why, promo)) return invalid("v_cache: " + why);
 
   dec::Params p;
   p.q = a.q;

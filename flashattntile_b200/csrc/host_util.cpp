@@ -82,7 +82,7 @@ int sm_count(int device) {
 
 bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
                   const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle,
-                  std::string* why) {
+                  std::string* why, CUtensorMapL2promotion promotion) {
   EncodeFn fn = resolve_encode();
   if (fn == nullptr) {
     *why = "cuTensorMapEncodeTiled is not available from the CUDA driver";
@@ -99,7 +99,7 @@ bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const v
     if (i + 1 < rank) gstride[i] = strides_bytes[i];
   }
   CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdim, gstride, bdim, estride,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promotion,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     *why = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));

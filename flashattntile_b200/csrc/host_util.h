@@ -30,8 +30,10 @@ cudaError_t ensure_smem_limit(const void* func, int bytes, int device);
 
 // cuTensorMapEncodeTiled resolved through cudaGetDriverEntryPoint.
 // dims/strides are innermost-first; strides[i] is the byte stride of dim i+1.
+// `promotion` widens each L2 fill (use 128 B when a box row is only 128 B wide,
+// so neighbouring rows of other heads are not fetched along).
 bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
                   const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle,
-                  std::string* why);
+                  std::string* why, CUtensorMapL2promotion promotion = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 
 }  // namespace fat
