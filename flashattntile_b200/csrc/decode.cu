@@ -41,7 +41,8 @@ namespace dec {
 constexpr int kWarps = 4;                  // consumer warps
 constexpr int kProducers = 2;              // producer warps (take turns by chunk)
 constexpr int kThreads = (kWarps + kProducers) * 32;
-constexpr int kChunk = 16 * kWarps;        // tokens per pipeline stage
+constexpr int kMaxChunk = 256;             // largest chunk (tokens per pipeline stage) of any layout
+constexpr int kMaxBoxes = 32;              // TMA row boxes per chunk at most (chunk / 8)
 constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
 constexpr int kStageBudget = 160 * 1024;   // shared memory for the stage ring
 
@@ -58,7 +59,7 @@ struct RingInfo {
   int b, unit_local, chunk, len, chunks_b, nbox;
   long long S;
 };
-constexpr int kRingBytes = kRing * int(sizeof(RingInfo)) + kRing * 8 * 4 * 3;
+constexpr int kRingBytes = kRing * int(sizeof(RingInfo)) + kRing * kMaxBoxes * 4 * 3;
 
 struct Meta {
   int flags;
@@ -68,8 +69,8 @@ struct Meta {
   int seq_len;
   int chunks_b;    // chunks per unit of this sequence
   long long unit_base;  // flattened index of the unit's first chunk
-  float kscale[kChunk / 8];
-  float vscale[kChunk / 8];
+  float kscale[kMaxChunk / 8];
+  float vscale[kMaxChunk / 8];
 };
 
 struct Params {
@@ -97,6 +98,10 @@ struct Layout {
   static constexpr int kRowBytes = D * EB;                         // one token row of one KV head
   static constexpr int kBoxBytes = kRowBytes >= 128 ? 128 : kRowBytes;  // TMA box row
   static constexpr int kCB = kRowBytes / kBoxBytes;                // column boxes per row
+  // Tokens per consumer warp per stage: stages stay 32 KB (K + V) for narrow rows.
+  static constexpr int kTW = kRowBytes >= 256 ? 16 : (kRowBytes >= 128 ? 32 : 64);
+  static constexpr int kChunk = kWarps * kTW;                      // tokens per pipeline stage
+  static_assert(kChunk <= kMaxChunk, "chunk larger than the per-stage metadata");
   static constexpr int kTile = kChunk * kRowBytes;                 // K (or V) bytes per stage
   static constexpr int kStage = 2 * kTile;
   static constexpr int kStages = (kStageBudget / kStage) > 8 ? 8 : (kStageBudget / kStage);
@@ -207,6 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int EB = (KVT == FAT_DTYPE_I8 || KVT == FAT_DTYPE_E4M3) ? 1 : 2;
   using L = Layout<D, EB>;
   constexpr int kStages = L::kStages;
+  constexpr int kChunk = L::kChunk;
+  constexpr int kTW = L::kTW;
   constexpr int NT = D / 8;  // n-tiles of the output
 
   extern __shared__ uint8_t smem_raw[];
@@ -319,8 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int own_issued = 0;
     RingInfo* rinfo = reinterpret_cast<RingInfo*>(ring_base + pid * kRingBytes);
     int* rids = reinterpret_cast<int*>(rinfo + kRing);
-    float* rks = reinterpret_cast<float*>(rids + kRing * 8);
-    float* rvs = rks + kRing * 8;
+    float* rks = reinterpret_cast<float*>(rids + kRing * kMaxBoxes);
+    float* rvs = rks + kRing * kMaxBoxes;
     if (n_own > 0) {
       // The walk keeps (sequence, unit, chunk) incrementally, so the loop does
       // no 64-bit division (emulated and slow on the GPU).
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (lane < nbox) {
             const int lp = (tok0 + lane * p.box_rows) / p.page_size;
-            int* dst = rids + r * 8 + lane;
+            int* dst = rids + r * kMaxBoxes + lane;
             if (lp < p.max_pages) {
               cp_async_4(smem_u32(dst), p.page_table + (long long)wb * p.pt_sb + lp);
             } else {
@@ -390,10 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int nbox = rinfo[r].nbox;
             const int kvh = rinfo[r].unit_local / p.head_groups;
             if (lane < nbox) {
-              const int ph = rids[r * 8 + lane];
+              const int ph = rids[r * kMaxBoxes + lane];
               if (ph >= 0 && ph < p.num_pages) {
-                cp_async_4(smem_u32(rks + r * 8 + lane), p.k_scale + (long long)ph * p.s_sp + kvh);
-                cp_async_4(smem_u32(rvs + r * 8 + lane), p.v_scale + (long long)ph * p.s_sp + kvh);
+                cp_async_4(smem_u32(rks + r * kMaxBoxes + lane), p.k_scale + (long long)ph * p.s_sp + kvh);
+                cp_async_4(smem_u32(rvs + r * kMaxBoxes + lane), p.v_scale + (long long)ph * p.s_sp + kvh);
               }
             }
           }
@@ -434,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tok0 = chunk * kChunk;
         int phys = -1;
         if (lane < nbox) {
-          phys = rids[r * 8 + lane];
+          phys = rids[r * kMaxBoxes + lane];
           if (phys < 0 || phys >= p.num_pages) {
             raise_error(p.err, FAT_DEVERR_BAD_PAGE);
             phys = -1;
@@ -446,10 +453,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // One scale pair per 8-token group of the chunk; groups past the
           // sequence end (or on a rejected page) get 0 so that masked tokens
           // never meet stale shared memory.
-          const float ksc = phys >= 0 ? rks[r * 8 + lane] : 0.f;
-          const float vsc = phys >= 0 ? rvs[r * 8 + lane] : 0.f;
+          const float ksc = phys >= 0 ? rks[r * kMaxBoxes + lane] : 0.f;
+          const float vsc = phys >= 0 ? rvs[r * kMaxBoxes + lane] : 0.f;
           const int per8 = p.box_rows / 8;  // 8-token groups per box
-          const int src = (lane & 7) / per8;
+          const int src = lane / per8;
           const float kg = __shfl_sync(0xffffffffu, ksc, src);
           const float vg = __shfl_sync(0xffffffffu, vsc, src);
           if (lane < kChunk / 8) {
@@ -490,10 +497,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // One TMA copy per (row box, K|V): the box spans every 128-byte column
         // block of its rows (5-D map), landing as [rows][row bytes] in the stage.
         const uint32_t st = smem_u32(stages) + uint32_t(s) * L::kStage;
-        {
-          const int box = lane >> 1, tensor = lane & 1;
-          const int ph = __shfl_sync(0xffffffffu, phys, box & 7);
-          if (box < nbox && ph >= 0) {
+        for (int j0 = 0; j0 < 2 * nbox; j0 += 32) {
+          const int j = j0 + lane;
+          const int box = j >> 1, tensor = j & 1;
+          const int ph = __shfl_sync(0xffffffffu, phys, box & 31);
+          if (j < 2 * nbox && ph >= 0) {
             const int t = tok0 + box * p.box_rows;
             const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(box * p.box_rows * L::kRowBytes);
             tma_load_5d(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph);
@@ -559,10 +567,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    const int tok0 = chunk * kChunk + warp * 16;
-    const int nvalid = seq_len - tok0;
     const uint32_t kt = smem_u32(stages) + uint32_t(s) * L::kStage;
     const uint32_t vt = kt + L::kTile;
+    // Each warp owns kTW consecutive tokens of the chunk, done 16 at a time.
+#pragma unroll 1
+    for (int sub = 0; sub < kTW / 16; ++sub) {
+    const int wrow = warp * kTW + sub * 16;  // first row of this slice in the stage
+    const int tok0 = chunk * kChunk + wrow;
+    const int nvalid = seq_len - tok0;
     if (nvalid > 0) {
       if (nvalid < 16) {
         // Rows past the sequence may hold anything (even NaN): zero their V so
@@ -571,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = lane; i < (16 - nvalid) * kVecPerRow; i += 32) {
           const int r = nvalid + i / kVecPerRow;
           const int bc = (i % kVecPerRow) * 16;
-          const uint32_t a = L::addr(vt, warp * 16 + r, bc);
+          const uint32_t a = L::addr(vt, wrow + r, bc);
           asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
         }
         __syncwarp();
@@ -582,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 2; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
       if constexpr (EB == 2) {
-        const int row = warp * 16 + ((lane >> 4) << 3) + (lane & 7);
+        const int row = wrow + ((lane >> 4) << 3) + (lane & 7);
         const int khalf = ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
@@ -601,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kSlice = D / 4;  // bytes per lane per row
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const int row = warp * 16 + j * 8 + g;
+          const int row = wrow + j * 8 + g;
 #pragma unroll
           for (int v = 0; v < kSlice / 16 + (kSlice % 16 ? 1 : 0); ++v) {
             uint32_t wv[4];
@@ -632,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float sv[4];
       float ksc[2] = {1.f, 1.f}, vsc[2] = {1.f, 1.f};
       if constexpr (EB == 1) {
-        const int grp = (warp * 16) / 8;
+        const int grp = (wrow) / 8;
         ksc[0] = mt.kscale[grp];
         ksc[1] = mt.kscale[grp + 1];
         vsc[0] = mt.vscale[grp];
@@ -665,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       split_hi_lo<T>(pr[0] * vsc[0], pr[1] * vsc[0], pa[0], pa[1]);
       split_hi_lo<T>(pr[2] * vsc[1], pr[3] * vsc[1], pa[2], pa[3]);
       if constexpr (EB == 2) {
-        const int row = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        const int row = wrow + ((lane >> 3) & 1) * 8 + (lane & 7);
         const int dsel = (lane >> 4) << 3;
 #pragma unroll
         for (int np = 0; np < D / 16; ++np) {
@@ -679,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // of n-tile nt is dim g*D/8 + nt) and reads token rows 2c, 2c+1, 2c+8,
         // 2c+9; byte nt of two rows forms the pair of one B register.
         constexpr int kSlice = D / 8;  // bytes per lane per row
-        const int rbase = warp * 16 + 2 * c;
+        const int rbase = wrow + 2 * c;
         uint32_t rw[4][kSlice / 4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -710,6 +722,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (nvalid < 16) fence_proxy_async_smem();
+    }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8u * s);
@@ -874,7 +887,7 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   // One TMA box covers gcd(page_size, chunk) token rows -- as tall as possible
   // (whole pages up to the 64-token chunk) while never crossing a page or a
   // chunk boundary, so large pages need fewer, taller copies.
-  int box_rows = dec::kChunk;
+  int box_rows = L::kChunk;
   while (a.page_size % box_rows) box_rows >>= 1;
   // 5-D view of the cache: {elements of a 128-byte column block, column block,
   // kv head, slot, page}; one box = box_rows slots x every column block of one
