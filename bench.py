@@ -287,7 +287,7 @@ def main() -> None:
     e2e_ok = torch.allclose(o_h.to(device).float(), out.float(), atol=0, rtol=0)
 
     secondary = {}
-    if not args.no_secondary:
+    if not args.no_secondary and world == 1:
         secondary = run_secondary(device, args, peaks)
     if dist is not None:
         dist.barrier()
