@@ -18,7 +18,9 @@ metric = decode HBM GB/s = algorithmic bytes (Q + K + V + O, FlashAttnTile's
 * ``cpu_baseline``: the numpy restatement of the reference's fp32 path
   (oracle/) on the same cfg2 inputs, timed on this host's cores.
 * ``secondary``: the other hot-path kernels measured the same way (quantised
-  decode cfg4, varlen prefill cfg3 when built).
+  decode cfg4 and varlen prefill cfg3 at N=1; the cfg5 long-context decode
+  split by page range across the N ranks, with its NCCL exchange and LSE
+  merge, at every N).
 
 Multi-GPU (torchrun, one rank per GPU): decode shards by (sequence, KV head)
 with no communication; every rank owns a cfg2-sized shard (weak scaling) and
@@ -196,7 +198,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--only", choices=["decode", "quant", "prefill"], default=None,
+    ap.add_argument("--only", choices=["decode", "quant", "prefill", "longctx"], default=None,
                     help="run one workload (profiling); decode = the headline line without secondary")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -224,8 +226,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     peaks = _peaks()
-    if args.only in ("quant", "prefill"):
-        res = run_secondary(device, args, peaks, which=(args.only,))
+    if args.only in ("quant", "prefill", "longctx"):
+        res = run_secondary(device, args, peaks, which=(args.only,), dist=dist)
         if rank == 0:
             print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup, "results": res}),
                   flush=True)
@@ -287,8 +289,9 @@ def main() -> None:
     e2e_ok = torch.allclose(o_h.to(device).float(), out.float(), atol=0, rtol=0)
 
     secondary = {}
-    if not args.no_secondary and world == 1:
-        secondary = run_secondary(device, args, peaks)
+    if not args.no_secondary:
+        which = ("quant", "prefill", "longctx") if world == 1 else ("longctx",)
+        secondary = run_secondary(device, args, peaks, which=which, dist=dist)
     if dist is not None:
         dist.barrier()
 
@@ -337,14 +340,89 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def run_secondary(device, args, peaks, which=("quant", "prefill")) -> dict:
-    """Quantised decode (cfg4) and varlen prefill (cfg3)."""
+def run_secondary(device, args, peaks, which=("quant", "prefill", "longctx"), dist=None) -> dict:
+    """Quantised decode (cfg4), varlen prefill (cfg3), long-context decode (cfg5)."""
     res = {}
     if "quant" in which:
         res.update(run_quant(device, args, peaks))
     if "prefill" in which:
         res.update(run_prefill(device, args, peaks))
+    if "longctx" in which:
+        res.update(run_longctx(device, args, peaks, dist))
     return res
+
+
+CFG5 = dict(batch=8, heads=64, kv_heads=8, head_dim=128, page_size=64, ctx=131072)
+
+
+def run_longctx(device, args, peaks, dist=None) -> dict:
+    """cfg5: B8, H64/8, D128, ps64, ctx 131072 fp16, pages split by range over the ranks.
+
+    Every rank holds logical pages [p0, p1) of every sequence in its own pool
+    (strong scaling: the total cache is fixed, 4.3 GB).  A step is the local
+    decode into fp32 partials, the NCCL all-gather of the packed partials and
+    the LSE merge; the time is the slowest rank's.  The metric counts the
+    whole job's algorithmic bytes (all ranks' K/V plus Q and O once)."""
+    from flashattntile_b200 import sequence_parallel as sp
+    from flashattntile_b200.paging import PagedKVCache
+
+    c = CFG5
+    world = dist.get_world_size() if dist is not None else 1
+    rank = dist.get_rank() if dist is not None else 0
+    pages_per_seq = c["ctx"] // c["page_size"]
+    p0, p1 = sp.page_range(pages_per_seq, world, rank)
+    local_pages = p1 - p0
+    pool = c["batch"] * local_pages
+    shape = (pool, c["page_size"], c["kv_heads"], c["head_dim"])
+    gen = torch.Generator(device=device).manual_seed(50 + rank)
+    k = torch.empty(shape, dtype=torch.float16, device=device)
+    v = torch.empty_like(k)
+    for i in range(0, pool, 1024):
+        k[i:i + 1024].normal_(generator=gen)
+        v[i:i + 1024].normal_(generator=gen)
+    gq = torch.Generator(device=device).manual_seed(49)  # same q on every rank
+    q = torch.randn((c["batch"], c["heads"], c["head_dim"]), generator=gq, device=device).half()
+    table = torch.randperm(pool, generator=gen, device=device).view(c["batch"], local_pages).to(torch.int32)
+    full_lens = torch.full((c["batch"],), c["ctx"], dtype=torch.int32, device=device)
+    cache = PagedKVCache(k, v, table, sp.local_lengths(full_lens, c["page_size"], p0, p1), c["page_size"])
+    packed = torch.empty(sp.packed_size(c["batch"], c["heads"], c["head_dim"]), dtype=torch.float32, device=device)
+    parts = torch.empty((world, packed.numel()), dtype=torch.float32, device=device)
+    out = torch.empty_like(q)
+    total_bytes = decode_bytes([c["ctx"]] * c["batch"], c["heads"], c["kv_heads"], c["head_dim"], c["page_size"])
+
+    def step():
+        sp.decode_partial(q, cache, packed=packed)
+        if dist is not None:
+            sp.exchange_partials(packed, out=parts)
+        else:
+            parts.copy_(packed.view(1, -1))
+        sp.merge_partials(parts, c["batch"], c["heads"], c["head_dim"], torch.float16, out=out)
+
+    from flashattntile_b200._config import value_checks
+
+    steps = max(10, args.steps // 2)
+    with value_checks(False):  # no host syncs inside the timed loop
+        if dist is not None:
+            dist.barrier()
+        times = time_steps(step, steps, args.warmup, None)
+        decode_times = time_steps(lambda: sp.decode_partial(q, cache, packed=packed), steps, args.warmup, None)
+    ms, dms = statistics.mean(times), statistics.mean(decode_times)
+    if dist is not None:
+        t = torch.tensor([ms, dms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, dms = (float(x) for x in t.tolist())
+    local_bytes = decode_bytes([c["ctx"] // world] * c["batch"], c["heads"], c["kv_heads"], c["head_dim"],
+                               c["page_size"])
+    del k, v, cache
+    torch.cuda.empty_cache()
+    return {"cfg5_longctx_decode": {
+        "value": round(total_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms": round(ms, 4), "n_gpus": world,
+        "scaling": "strong", "algorithmic_bytes": total_bytes,
+        "local_decode_ms": round(dms, 4),
+        "local_decode_frac_hbm": round(local_bytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+        "exchange_bytes_per_rank": packed.numel() * 4,
+        "step": "decode partial + NCCL all_gather_into_tensor + LSE merge" if world > 1
+                else "decode partial + LSE merge (1 part)"}}
 
 
 def run_quant(device, args, peaks) -> dict:

@@ -55,6 +55,12 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,
          _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp],
     ),
+    "fat_paged_decode_lse": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,
+         _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp],
+    ),
+    "fat_lse_merge": (_i32, [_vp, _i64, _vp, _i64, _i32, _i64, _i32, _vp, _i32, _vp, _vp]),
     "fat_paged_decode_noalloc": (
         _i32,
         [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,

@@ -5,6 +5,7 @@
 
 #include "decode.h"
 #include "gather.h"
+#include "merge.h"
 #include "prefill.h"
 #include "host_util.h"
 
@@ -18,14 +19,15 @@ size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int
   return fat::decode_workspace_bytes(device, batch, num_heads, num_kv_heads, head_dim);
 }
 
-int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
-                     const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
-                     int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
-                     const int32_t* seq_lens, const float* k_scale, const float* v_scale,
-                     int64_t scale_stride_page, void* out, int64_t out_stride_b, int64_t out_stride_h, int batch,
-                     int num_heads, int num_kv_heads, int head_dim, int page_size, int q_dtype, int kv_dtype,
-                     int out_dtype, float softmax_scale, int split_k_hint, void* workspace, size_t workspace_bytes,
-                     int32_t* error_word, void* stream) {
+namespace {
+int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+                 int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head, int64_t num_pages,
+                 const int32_t* page_table, int64_t page_table_stride, int64_t max_pages, const int32_t* seq_lens,
+                 const float* k_scale, const float* v_scale, int64_t scale_stride_page, void* out,
+                 int64_t out_stride_b, int64_t out_stride_h, float* lse, int64_t lse_stride_b, int batch,
+                 int num_heads, int num_kv_heads, int head_dim, int page_size, int q_dtype, int kv_dtype,
+                 int out_dtype, float softmax_scale, int split_k_hint, void* workspace, size_t workspace_bytes,
+                 int32_t* error_word, void* stream) {
   fat::set_last_error("");
   if (split_k_hint < 1 || split_k_hint > 64)
     return fat::invalid("paged_decode: split_k must be in [1, 64], got " + std::to_string(split_k_hint));
@@ -62,7 +64,63 @@ int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, cons
   a.workspace_bytes = workspace_bytes;
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
+  a.lse = lse;
+  a.lse_sb = lse_stride_b;
   return fat::launch_paged_decode(a);
+}
+}  // namespace
+
+int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
+                     const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                     int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                     const int32_t* seq_lens, const float* k_scale, const float* v_scale,
+                     int64_t scale_stride_page, void* out, int64_t out_stride_b, int64_t out_stride_h, int batch,
+                     int num_heads, int num_kv_heads, int head_dim, int page_size, int q_dtype, int kv_dtype,
+                     int out_dtype, float softmax_scale, int split_k_hint, void* workspace, size_t workspace_bytes,
+                     int32_t* error_word, void* stream) {
+  return decode_entry(q, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_slot, kv_stride_head,
+                      num_pages, page_table, page_table_stride, max_pages, seq_lens, k_scale, v_scale,
+                      scale_stride_page, out, out_stride_b, out_stride_h, nullptr, 0, batch, num_heads,
+                      num_kv_heads, head_dim, page_size, q_dtype, kv_dtype, out_dtype, softmax_scale, split_k_hint,
+                      workspace, workspace_bytes, error_word, stream);
+}
+
+int fat_paged_decode_lse(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
+                         const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                         int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                         const int32_t* seq_lens, const float* k_scale, const float* v_scale,
+                         int64_t scale_stride_page, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                         float* lse, int64_t lse_stride_b, int batch, int num_heads, int num_kv_heads, int head_dim,
+                         int page_size, int q_dtype, int kv_dtype, int out_dtype, float softmax_scale,
+                         int split_k_hint, void* workspace, size_t workspace_bytes, int32_t* error_word,
+                         void* stream) {
+  if (lse == nullptr) {
+    fat::set_last_error("paged_decode_lse: lse must not be null");
+    return FAT_ERR_INVALID_ARGUMENT;
+  }
+  return decode_entry(q, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_slot, kv_stride_head,
+                      num_pages, page_table, page_table_stride, max_pages, seq_lens, k_scale, v_scale,
+                      scale_stride_page, out, out_stride_b, out_stride_h, lse, lse_stride_b, batch, num_heads,
+                      num_kv_heads, head_dim, page_size, q_dtype, kv_dtype, out_dtype, softmax_scale, split_k_hint,
+                      workspace, workspace_bytes, error_word, stream);
+}
+
+int fat_lse_merge(const float* o, int64_t o_part_stride, const float* lse, int64_t lse_part_stride, int parts,
+                  int64_t rows, int head_dim, void* out, int out_dtype, float* lse_out, void* stream) {
+  fat::set_last_error("");
+  fat::MergeArgs a;
+  a.o = o;
+  a.o_part_stride = o_part_stride;
+  a.lse = lse;
+  a.lse_part_stride = lse_part_stride;
+  a.parts = parts;
+  a.rows = rows;
+  a.head_dim = head_dim;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.lse_out = lse_out;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return fat::launch_lse_merge(a);
 }
 
 int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,

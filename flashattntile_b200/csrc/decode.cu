@@ -87,6 +87,8 @@ struct Params {
   int batch, num_heads, num_kv_heads, group, head_groups, page_size, num_pages, box_rows, max_pages;
   float scale_log2;
   int out_f32;
+  float* lse;    // optional [batch][num_heads] (stride lse_sb): m + log2(l), base-2 log-sum-exp
+  long long lse_sb;
   float* ws_o;   // [grid][2][kRows][D]
   float* ws_ml;  // [grid][2][kRows][2]
   int* ws_count; // [units]
@@ -303,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         reinterpret_cast<T*>(p.out)[off] = from_float<T>(0.f);
       }
+      if (p.lse != nullptr && d == 0) p.lse[(long long)b * p.lse_sb + h] = -CUDART_INF_F;
     }
   }
 
@@ -774,6 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
           }
+          if (p.lse != nullptr && d == 0) p.lse[(long long)b * p.lse_sb + h0 + gg] = M + __log2f(Lsum);
         } else {
           const long long base = ((long long)blockIdx.x * 2 + slot) * kRows + gg;
           p.ws_o[base * D + d] = O;
@@ -830,6 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
             }
+            if (p.lse != nullptr && d == 0) p.lse[(long long)b * p.lse_sb + h0 + gg] = M + __log2f(Lsum);
           }
           // Leave the whole workspace zero-filled for the next call, whatever
           // its shape: the (m, l) pairs once every thread has read them, then
@@ -937,6 +942,8 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   p.ws_ml = reinterpret_cast<float*>(wsb + ws.ml_off);
   p.ws_count = reinterpret_cast<int*>(wsb + ws.count_off);
   p.err = a.error_word;
+  p.lse = a.lse;
+  p.lse_sb = a.lse_sb;
   (void)device;
   kern<<<grid, dec::kThreads, L::kSmem, a.stream>>>(tmk, tmv, p);
   e = cudaGetLastError();

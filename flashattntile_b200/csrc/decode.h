@@ -29,6 +29,8 @@ struct DecodeArgs {
   size_t workspace_bytes;
   int32_t* error_word;
   cudaStream_t stream;
+  float* lse = nullptr;  // optional [batch, num_heads] base-2 log-sum-exp of the scaled scores
+  int64_t lse_sb = 0;
 };
 
 // Scratch bytes for one decode problem: per-CTA split partials + one ticket per unit.

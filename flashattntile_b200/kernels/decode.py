@@ -93,8 +93,12 @@ def _aligned_q(q: torch.Tensor) -> torch.Tensor:
 
 
 def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
-                  k_scale=None, v_scale=None, out=None, out_dtype=None):
+                  k_scale=None, v_scale=None, out=None, out_dtype=None, lse=None):
     """Run ``fat_paged_decode`` on the current stream of q's device.
+
+    With ``lse`` (fp32 ``[B, H]``, unit stride along H) the kernel also writes
+    the base-2 log-sum-exp of each row's scaled scores (``fat_paged_decode_lse``),
+    -inf for a sequence with no cached tokens.
 
     No host<->device synchronisation happens here; device-side problems are
     recorded in the stream's error word (``flashattntile_b200.device_error``).
@@ -128,14 +132,22 @@ def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_
     args = (q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
             k_cache.stride(1), k_cache.stride(2), k_cache.shape[0], page_table.data_ptr(), page_table.stride(0),
             page_table.shape[1], seq_lens.data_ptr(), _lib.ptr(k_scale), _lib.ptr(v_scale), scale_stride,
-            out.data_ptr(), out.stride(0), out.stride(1), batch, heads, kvh, dim, int(page_size),
-            _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[k_cache.dtype], _lib.DTYPE_CODE[out_dtype],
-            float(softmax_scale), int(split_k), ws.data_ptr(), ws.numel(), err.data_ptr(), stream)
+            out.data_ptr(), out.stride(0), out.stride(1))
+    tail = (batch, heads, kvh, dim, int(page_size), _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[k_cache.dtype],
+            _lib.DTYPE_CODE[out_dtype], float(softmax_scale), int(split_k), ws.data_ptr(), ws.numel(),
+            err.data_ptr(), stream)
+    if lse is None:
+        fn, args = lib.fat_paged_decode, args + tail
+    else:
+        if lse.dtype != torch.float32 or lse.device != dev or lse.dim() != 2 or lse.stride(1) != 1 \
+                or tuple(lse.shape) != (batch, heads):
+            raise ValueError(f"lse must be a float32 [{batch}, {heads}] tensor on {dev} with unit stride along heads")
+        fn, args = lib.fat_paged_decode_lse, args + (lse.data_ptr(), lse.stride(0)) + tail
     if idx == torch.cuda.current_device():
-        status = lib.fat_paged_decode(*args)
+        status = fn(*args)
     else:
         with torch.cuda.device(idx):
-            status = lib.fat_paged_decode(*args)
+            status = fn(*args)
     _lib.check(status, "paged_decode")
     return out
 

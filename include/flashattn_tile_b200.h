@@ -99,6 +99,36 @@ int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, cons
                      int32_t* error_word, void* stream);
 
 /*
+ * fat_paged_decode that also writes, per (sequence, query head), the base-2
+ * log-sum-exp of the scaled scores, lse[b * lse_stride_b + h] = m + log2(l)
+ * (-inf for a sequence with no cached tokens).  With out_dtype F32 the pair
+ * (out, lse) is the partial a sequence-parallel decode exchanges: decode each
+ * GPU's own key range (a page-table column slice with per-GPU lengths), gather
+ * the partials, combine them with fat_lse_merge.  Replaces the split-K partial
+ * outputs of FlashAttnTile's _decode_paged_split_kernel (kernels/decode.py:223-313).
+ */
+int fat_paged_decode_lse(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache,
+                         const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                         int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                         const int32_t* seq_lens, const float* k_scale, const float* v_scale,
+                         int64_t scale_stride_page, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                         float* lse, int64_t lse_stride_b, int batch, int num_heads, int num_kv_heads, int head_dim,
+                         int page_size, int q_dtype, int kv_dtype, int out_dtype, float softmax_scale,
+                         int split_k_hint, void* workspace, size_t workspace_bytes, int32_t* error_word,
+                         void* stream);
+
+/*
+ * Merge `parts` attention partials over disjoint key ranges:
+ *   out[row] = sum_r o[r][row] 2^(lse[r][row] - M) / sum_r 2^(lse[r][row] - M),  M = max_r lse[r][row]
+ * o: fp32 [parts][rows][head_dim] (part r at o + r * o_part_stride), lse: fp32 [parts][rows]
+ * (part r at lse + r * lse_part_stride), out: [rows][head_dim] of out_dtype (F16 | BF16 | F32),
+ * lse_out: optional [rows] merged log-sum-exp.  Rows whose parts are all -inf give zeros.
+ * Replaces FlashAttnTile's _decode_reduce_kernel (kernels/decode.py:316-356).
+ */
+int fat_lse_merge(const float* o, int64_t o_part_stride, const float* lse, int64_t lse_part_stride, int parts,
+                  int64_t rows, int head_dim, void* out, int out_dtype, float* lse_out, void* stream);
+
+/*
  * fat_paged_decode for callers that cannot allocate device memory.  No
  * counterpart exists in the reference: it is an addition for engines that
  * allocate every device buffer up front and forbid allocation afterwards,
