@@ -1,26 +1,31 @@
 // Packed varlen prefill attention (causal or not, GQA/MQA) for sm_100a.
 //
 // Replaces FlashAttnTile's _fwd_varlen_kernel (flashattn_tile/kernels/prefill.py:34-138):
-// per (128-row query tile, query head, sequence) an online-softmax pass over
-// 128-row K/V tiles with bottom-right causal alignment (query i sees keys
+// per (query tile, query head, sequence) an online-softmax pass over 128-row
+// K/V tiles with bottom-right causal alignment (query i sees keys
 // j <= i + kv_len - q_len), GQA head h reading KV head h / G, P rounded to the
 // input dtype before P.V (prefill.py:128) and fp32 accumulation.
 //
-// One CTA per query tile, warp-specialised:
-//   warp 4      TMA producer: the Q tile once, then K and V tiles into two
-//               independent 128-byte-swizzled rings (K released after Q.K^T,
-//               V after P.V);
-//   warp 5      tcgen05 issuer (one thread): S_j = Q K_j^T into one of two
-//               tensor-memory S buffers, then O += P_{j-1} V_{j-1} with P read
-//               straight from tensor memory, so the next Q.K^T overlaps the
-//               softmax of the previous tile;
-//   warps 0-3   softmax: thread r owns query row r (tensor-memory lane r), reads
+// One CTA per pair of 128-row query tiles (256 rows), warp-specialised:
+//   warps 0-3   softmax of query tile 0, warps 4-7 softmax of query tile 1:
+//               thread r owns row r of its tile (tensor-memory lane r), reads
 //               its S row, keeps the running max and sum in registers, writes P
-//               (16-bit) over its S row, and rescales O in tensor memory only
-//               when the row max grew by more than 2^8 (P stays <= 256).
-// Accumulators live in tensor memory: S0, S1 (128 columns each) and O (head_dim
-// columns).  Every wait is bounded; on a timeout the CTA records
-// FAT_DEVERR_TIMEOUT, drains its copies and MMAs, frees tensor memory and exits.
+//               (16-bit) over its S row, and rescales its O row in tensor
+//               memory only when the row max grew by more than 2^8 (P <= 256);
+//   warp 8      TMA producer: both Q tiles once, then K and V tiles into two
+//               independent 128-byte-swizzled rings;
+//   warp 9      tcgen05 issuer (one thread), per K/V tile j:
+//                 O0 += P0 V_{j-1};  S0 = Q0 K_j^T;  O1 += P1 V_{j-1};  S1 = Q1 K_j^T
+//               so the tensor core works on one tile while the other tile's
+//               softmax runs (ping-pong between the two warpgroups);
+//   warps 10-11 idle (they complete the third warpgroup for setmaxnreg).
+// Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D),
+// O1 [384,384+D).  P_t is written over S_t; S_t(j) is issued after O_t += P_t(j-1)
+// V_{j-1} by the same thread, and tcgen05.mma operations of one thread execute
+// in issue order, so the completion of S_t(j) also means O_t holds every
+// earlier P.V (the softmax may rescale O_t as soon as it sees S_t(j)).
+// Every wait is bounded; on a timeout the CTA records FAT_DEVERR_TIMEOUT,
+// drains its copies and MMAs, frees tensor memory and exits.
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -31,13 +36,21 @@
 namespace fat {
 namespace pre {
 
-constexpr int BM = 128;  // query rows per CTA
-constexpr int BN = 128;  // keys per K/V tile
-constexpr int kSoftmaxWarps = 4;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
+constexpr int BM = 128;    // query rows per tile (the MMA's M)
+constexpr int BN = 128;    // keys per K/V tile
+constexpr int kTiles = 2;  // query tiles per CTA
+constexpr int kRowsPerCta = BM * kTiles;
+constexpr int kSoftmaxThreads = 128;  // per tile
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 12 * 32;
 constexpr uint32_t kTmemCols = 512;
+// Register split: launched at 168 per thread (65536 / 384, rounded to 8); the
+// third warpgroup (producer, MMA, 2 idle warps) drops to 88 and the two
+// softmax warpgroups rise to 208: 2*128*208 + 128*88 = 64512 = 384 * 168.
+constexpr int kRegsSoftmax = 208;
+constexpr int kRegsOther = 88;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * 168, "register split exceeds the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 without rescaling
 
 struct Params {
@@ -54,15 +67,39 @@ struct Params {
 
 template <int D>
 struct Layout {
-  static constexpr int kCB = D / 64;            // 128-byte column blocks (16-bit elements)
-  static constexpr int kTile = BM * D * 2;      // one Q, K or V tile
+  static constexpr int kCB = D / 64;        // 128-byte column blocks (16-bit elements)
+  static constexpr int kTile = BM * D * 2;  // one Q, K or V tile
   static constexpr int kStagesK = D <= 64 ? 4 : 3;
-  static constexpr int kStagesV = D <= 64 ? 4 : 3;
-  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 + 2 + 3) + 16;
-  static constexpr size_t kSmem = 1024 + size_t(kTile) * (1 + kStagesK + kStagesV) + kBarBytes;
-  static constexpr uint32_t kColS = 0;    // S_b at column kColS + 128 b
-  static constexpr uint32_t kColO = 256;  // O at columns [256, 256 + D)
+  static constexpr int kStagesV = D <= 64 ? 4 : 2;
+  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 2 * kTiles + 1) + 16;
+  static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
+  static constexpr uint32_t kColS = 0;    // S_t at column kColS + 128 t
+  static constexpr uint32_t kColO = 256;  // O_t at columns [256 + 128 t, 256 + 128 t + D)
 };
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+template <int Regs>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Regs));
+}
+template <int Regs>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Regs));
+}
+
+// Number of K/V tiles query tile `t` of the CTA needs (0 if the tile is empty).
+__device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int causal) {
+  if (m0 >= q_len || kv_len <= 0) return 0;
+  const int n_kv = (kv_len + BN - 1) / BN;
+  if (!causal) return n_kv;
+  const int lim = min(m0 + BM, q_len) - 1 + (kv_len - q_len);  // last key any row of the tile sees
+  return lim < 0 ? 0 : min(n_kv, lim / BN + 1);
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -76,37 +113,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int h = blockIdx.x % p.num_heads;
   const int b = blockIdx.x / p.num_heads;
-  const int m_tile = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
+  const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
   const int q0 = __ldg(p.cu_q + b), q_len = __ldg(p.cu_q + b + 1) - q0;
   const int k0 = __ldg(p.cu_k + b), kv_len = __ldg(p.cu_k + b + 1) - k0;
-  const int m0 = m_tile * BM;
+  const int m0 = pair * kRowsPerCta;
   if (m0 >= q_len) return;  // uniform for the CTA, before any barrier or allocation
   const int kvh = h / p.group;
   const int offset = kv_len - q_len;  // bottom-right causal alignment
-  int n_kv = kv_len > 0 ? (kv_len + BN - 1) / BN : 0;
-  if (p.causal) {
-    const int lim = min(m0 + BM, q_len) - 1 + offset;  // last key any row of the tile sees
-    n_kv = lim < 0 ? 0 : min(n_kv, lim / BN + 1);
-  }
+  const int n0 = tiles_needed(m0, q_len, kv_len, p.causal);
+  const int n1 = tiles_needed(m0 + BM, q_len, kv_len, p.causal);
+  const int n_max = max(n0, n1);
+  const int q_tiles = (m0 + BM < q_len) ? 2 : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + L::kTile;
+  const uint32_t sQ = smem_u32(smem);  // [kTiles] tiles
+  const uint32_t sK = sQ + kTiles * L::kTile;
   const uint32_t sV = sK + SK * L::kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(L::kTile) * (1 + SK + SV));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(L::kTile) * (kTiles + SK + SV));
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t q_full = bar0;
-  const uint32_t k_full = bar0 + 8;                 // [SK]
-  const uint32_t k_empty = k_full + 8 * SK;         // [SK]
-  const uint32_t v_full = k_empty + 8 * SK;         // [SV]
-  const uint32_t v_empty = v_full + 8 * SV;         // [SV]
-  const uint32_t s_full = v_empty + 8 * SV;         // [2]
-  const uint32_t p_full = s_full + 16;              // [2]
-  const uint32_t o_done = p_full + 16;              // PV completions
-  const uint32_t o_final = o_done + 8;              // after the last P.V
-  const uint32_t drain = o_final + 8;               // final MMA drain
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 7);
+  const uint32_t k_full = bar0 + 8;          // [SK]
+  const uint32_t k_empty = k_full + 8 * SK;  // [SK]
+  const uint32_t v_full = k_empty + 8 * SK;  // [SV]
+  const uint32_t v_empty = v_full + 8 * SV;  // [SV]
+  const uint32_t s_full = v_empty + 8 * SV;  // [kTiles]: S_t(j) complete (and every earlier MMA)
+  const uint32_t p_full = s_full + 8 * kTiles;  // [kTiles]: P_t(j) written, O_t rescaled
+  const uint32_t drain = p_full + 8 * kTiles;   // every MMA of the CTA complete
+  volatile uint32_t* tmem_slot =
+      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -124,12 +159,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(v_full + 8 * s, 1);
       mbar_init(v_empty + 8 * s, 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(s_full + 8 * s, 1);
-      mbar_init(p_full + 8 * s, kSoftmaxWarps * 32);
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(s_full + 8 * t, 1);
+      mbar_init(p_full + 8 * t, kSoftmaxThreads);
     }
-    mbar_init(o_done, 1);
-    mbar_init(o_final, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -139,17 +172,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kProducerWarp) {
-    // ============================ TMA producer ============================
-    int issued_k = 0, issued_v = 0;
-    if (lane == 0 && n_kv > 0) {
+  if (warp >= kProducerWarp) {
+    regs_dec<kRegsOther>();
+    if (warp == kProducerWarp && lane == 0 && n_max > 0) {
+      // ============================ TMA producer ============================
+      int issued_k = 0, issued_v = 0;
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(q_full, L::kTile);
+      mbar_arrive_expect_tx(q_full, q_tiles * L::kTile);
+      for (int t = 0; t < q_tiles; ++t)
 #pragma unroll
-      for (int cb = 0; cb < L::kCB; ++cb) tma_load_3d(sQ + cb * BM * 128, &tm_q, q_full, cb * 64, h, q0 + m0);
-      for (int j = 0; j < n_kv; ++j) {
+        for (int cb = 0; cb < L::kCB; ++cb)
+          tma_load_3d(sQ + t * L::kTile + cb * BM * 128, &tm_q, q_full, cb * 64, h, q0 + m0 + t * BM);
+      for (int j = 0; j < n_max; ++j) {
         const int sk = j % SK, sv = j % SV;
         if (!mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag)) break;
         mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
@@ -172,64 +208,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = max(0, issued_v - SV); j < issued_v; ++j)
           mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ============================ MMA issuer ============================
-    if (lane == 0 && n_kv > 0) {
-      auto issue_pv = [&](int i) -> bool {
-        const int sb = i & 1, sv = i % SV;
-        if (!mbar_wait_bounded(p_full + 8 * sb, (i >> 1) & 1, p.err, abort_flag)) return false;
-        if (!mbar_wait_bounded(v_full + 8 * sv, (i / SV) & 1, p.err, abort_flag)) return false;
-        tc::fence_after_sync();
-        const uint32_t vbase = sV + sv * L::kTile;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bdesc = tc::sdesc_sw128(vbase + kk * 16 * 128, BN * 128, 1024);
-          tc::mma_ts(tmem + L::kColO, tmem + L::kColS + 128 * sb + kk * 8, bdesc, kIdescPV,
-                     (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc::commit(v_empty + 8 * sv);
-        tc::commit(o_done);
-        return true;
-      };
+    } else if (warp == kMmaWarp && lane == 0 && n_max > 0) {
+      // ============================ MMA issuer ============================
       bool ok = mbar_wait_bounded(q_full, 0, p.err, abort_flag);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int sb = j & 1, sk = j % SK;
-        if (!mbar_wait_bounded(k_full + 8 * sk, (j / SK) & 1, p.err, abort_flag)) break;
-        // S buffer sb held P_{j-2}: wait until P.V of tile j-2 has consumed it.
-        if (j >= 2 && !mbar_wait_bounded(o_done, (j - 2) & 1, p.err, abort_flag)) break;
-        tc::fence_after_sync();
-        const uint32_t kbase = sK + sk * L::kTile;
+      for (int j = 0; ok && j <= n_max; ++j) {
+        if (j < n_max && !mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, p.err, abort_flag)) break;
+        bool v_ready = false, used_v = false;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          tc::mma_ss(tmem + L::kColS + 128 * sb, tc::sdesc_sw128(sQ + off, 16, 1024),
-                     tc::sdesc_sw128(kbase + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < kTiles; ++t) {
+          const uint32_t colS = tmem + L::kColS + 128 * t;
+          const int n_t = t == 0 ? n0 : n1;
+          if (j >= 1 && j - 1 < n_t) {
+            // O_t += P_t(j-1) V_{j-1}
+            const int i = j - 1, sv = i % SV;
+            if (!mbar_wait_bounded(p_full + 8 * t, i & 1, p.err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            if (!v_ready) {
+              if (!mbar_wait_bounded(v_full + 8 * sv, (i / SV) & 1, p.err, abort_flag)) {
+                ok = false;
+                break;
+              }
+              v_ready = true;
+            }
+            tc::fence_after_sync();
+            // Descriptor start addresses are in 16-byte units: adding a byte
+            // offset >> 4 to the low field moves the operand (no carry: the
+            // shared window is below 2^18 bytes).
+            const uint64_t vdesc = tc::sdesc_sw128(sV + sv * L::kTile, BN * 128, 1024);
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk)
+              tc::mma_ts(tmem + L::kColO + 128 * t, colS + kk * 8, vdesc + uint64_t((kk * 16 * 128) >> 4), kIdescPV,
+                         (i > 0 || kk > 0) ? 1u : 0u);
+            used_v = true;
+          }
+          if (j < n_t) {
+            // S_t(j) = Q_t K_j^T
+            tc::fence_after_sync();
+            const uint64_t kdesc = tc::sdesc_sw128(sK + (j % SK) * L::kTile, 16, 1024);
+            const uint64_t qdesc = tc::sdesc_sw128(sQ + t * L::kTile, 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t off = uint64_t(((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4);
+              tc::mma_ss(colS, qdesc + off, kdesc + off, kIdescQK, kk > 0 ? 1u : 0u);
+            }
+            tc::commit(s_full + 8 * t);
+          } else if (j == n_t && j > 0) {
+            // Last P.V of tile t issued: one more s_full phase tells its
+            // softmax warps that O_t is final.
+            tc::commit(s_full + 8 * t);
+          }
         }
-        tc::commit(k_empty + 8 * sk);
-        tc::commit(s_full + 8 * sb);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
-        }
+        if (!ok) break;
+        if (used_v) tc::commit(v_empty + 8 * ((j - 1) % SV));
+        if (j < n_max) tc::commit(k_empty + 8 * (j % SK));
       }
-      if (ok && !*abort_flag && issue_pv(n_kv - 1)) tc::commit(o_final);
       // Every MMA this thread issued has finished once `drain` completes.
       tc::commit(drain);
       mbar_wait_bounded(drain, 0, nullptr, nullptr);
     }
   } else {
-    // ============================ softmax warps ============================
-    const int row = tid;  // 0..127: query row of the tile and tensor-memory lane
-    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
-    const int q_idx = m0 + row;
+    regs_inc<kRegsSoftmax>();
+    // ============================ softmax warpgroups ============================
+    const int t = warp >> 2;              // query tile of this warpgroup
+    const int row = tid & 127;            // row of the tile = tensor-memory lane
+    const int n_t = t == 0 ? n0 : n1;
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const uint32_t colS = L::kColS + 128 * t, colO = L::kColO + 128 * t;
+    const uint32_t sbar = s_full + 8 * t, pbar = p_full + 8 * t;
+    const int q_idx = m0 + t * BM + row;
     // Last key this row may see (inclusive).
     const int lim = p.causal ? min(kv_len - 1, q_idx + offset) : kv_len - 1;
     float m_used = -CUDART_INF_F, l_sum = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_bounded(s_full + 8 * sb, (j >> 1) & 1, p.err, abort_flag)) {
+    for (int j = 0; j < n_t; ++j) {
+      if (!mbar_wait_bounded(sbar, j & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -238,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         uint32_t r[BN / 32][32];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + L::kColS + 128 * sb + 32 * c, r[c]);
+        for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + colS + 32 * c, r[c]);
         tc::wait_ld();
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
@@ -250,9 +304,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < BN; ++i) s[i] = (kv0 + i <= lim) ? s[i] : -CUDART_INF_F;
       }
-      float mx = -CUDART_INF_F;
+      float mx;
+      {
+        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+        for (int i = 4; i < BN; i += 8) {
+          a0 = max3(a0, s[i], s[i + 4]);
+          a1 = max3(a1, s[i + 1], s[i + 5]);
+          a2 = max3(a2, s[i + 2], s[i + 6]);
+          a3 = max3(a3, s[i + 3], s[i + 7]);
+        }
+        mx = fmaxf(max3(a0, a1, a2), a3);
+      }
       mx *= p.scale_log2;
       float factor = 1.f;
       bool grow = false;
@@ -263,44 +326,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         l_sum *= factor;
       }
       if (__any_sync(0xffffffffu, grow)) {
-        // O holds P.V of tiles < j: wait for the last of them, then rescale in place.
-        if (!mbar_wait_bounded(o_done, (j - 1) & 1, p.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
+        // S_t(j) is complete, so O_t holds every earlier P.V: rescale in place.
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
-          tc::ld32(lane_base + L::kColO + 32 * c, r);
+          tc::ld32(lane_base + colO + 32 * c, r);
           tc::wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          tc::st32(lane_base + L::kColO + 32 * c, r);
+          tc::st32(lane_base + colO + 32 * c, r);
         }
-        tc::wait_st();
       }
       const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
-      float rowsum = 0.f;
+      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c) {
         uint32_t packed[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 32; i += 2) {
           const float p0 = fast_exp2(fmaf(s[64 * c + 2 * i], p.scale_log2, -msub));
           const float p1 = fast_exp2(fmaf(s[64 * c + 2 * i + 1], p.scale_log2, -msub));
-          rowsum += p0 + p1;
+          const float p2 = fast_exp2(fmaf(s[64 * c + 2 * i + 2], p.scale_log2, -msub));
+          const float p3 = fast_exp2(fmaf(s[64 * c + 2 * i + 3], p.scale_log2, -msub));
+          sum0 += p0;
+          sum1 += p1;
+          sum2 += p2;
+          sum3 += p3;
           packed[i] = pack2<T>(p0, p1);
+          packed[i + 1] = pack2<T>(p2, p3);
         }
-        tc::st32(lane_base + L::kColS + 128 * sb + 32 * c, packed);
+        tc::st32(lane_base + colS + 32 * c, packed);
       }
-      l_sum += rowsum;
+      l_sum += (sum0 + sum1) + (sum2 + sum3);
       tc::wait_st();
       tc::fence_before_sync();
-      mbar_arrive(p_full + 8 * sb);
+      mbar_arrive(pbar);
     }
-    // ---- epilogue: O / l -> global ----
-    if (ok && n_kv > 0 && mbar_wait_bounded(o_final, 0, p.err, abort_flag)) {
+    // ---- epilogue: O / l -> global, once the last P.V of this tile completed ----
+    if (ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag)) {
       tc::fence_after_sync();
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
       const bool store = q_idx < q_len;
@@ -308,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
-        tc::ld32(lane_base + L::kColO + 32 * c, r);
+        tc::ld32(lane_base + colO + 32 * c, r);
         tc::wait_ld();
         if (store) {
           if (p.out_f32) {
@@ -331,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    } else if (n_kv == 0 && q_idx < q_len) {
+    } else if (n_t == 0 && q_idx < q_len) {
       // No visible keys (only reachable with invalid causal inputs): zeros.
       const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
       for (int d = 0; d < D; ++d) {
@@ -397,8 +460,8 @@ int launch_t(const PrefillArgs& a) {
   p.causal = a.causal ? 1 : 0;
   p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
   p.err = a.error_word;
-  const int m_tiles = (a.max_seqlen_q + pre::BM - 1) / pre::BM;
-  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(m_tiles));
+  const int pairs = (a.max_seqlen_q + pre::kRowsPerCta - 1) / pre::kRowsPerCta;
+  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, pre::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill launch", e);
@@ -428,7 +491,7 @@ int launch_prefill_varlen(const PrefillArgs& a) {
   if (!aligned16(a.out) || (a.o_st * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16 ||
       (a.o_sh * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16)
     return unsupported("prefill_varlen: out must be 16-byte aligned with 16-byte-multiple strides");
-  if (a.max_seqlen_q > 65535 * pre::BM) return unsupported("prefill_varlen: max_seqlen_q too large");
+  if (a.max_seqlen_q > 65535 * pre::kRowsPerCta) return unsupported("prefill_varlen: max_seqlen_q too large");
   const bool bf = a.dtype == FAT_DTYPE_BF16;
   switch (a.head_dim) {
     case 64:
