@@ -69,9 +69,8 @@ SIGNATURES: dict[str, tuple] = {
     "fat_prefill_varlen": (
         _i32,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _i32, _i32,
-         _i32, _i32, _i32, _i32, _f32, _i32, _i32, _vp, _sz, _vp, _vp],
+         _i32, _i32, _i32, _i32, _f32, _i32, _i32, _vp, _vp],
     ),
-    "fat_prefill_workspace_size": (_sz, []),
     "fat_gather_paged": (
         _i32,
         [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp],

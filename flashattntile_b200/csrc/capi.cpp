@@ -60,8 +60,6 @@ int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const vo
   a.kv_dtype = kv_dtype;
   a.out_dtype = out_dtype;
   a.softmax_scale = softmax_scale;
-  a.workspace = workspace;
-  a.workspace_bytes = workspace_bytes;
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
   a.lse = lse;
@@ -128,8 +126,7 @@ int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
                        int64_t out_stride_t, int64_t out_stride_h, const int32_t* cu_seqlens_q,
                        const int32_t* cu_seqlens_k, int batch, int64_t total_q, int64_t total_k, int num_heads,
                        int num_kv_heads, int head_dim, int max_seqlen_q, int max_seqlen_k, int causal,
-                       float softmax_scale, int dtype, int out_dtype, void* workspace, size_t workspace_bytes,
-                       int32_t* error_word, void* stream) {
+                       float softmax_scale, int dtype, int out_dtype, int32_t* error_word, void* stream) {
   fat::set_last_error("");
   fat::PrefillArgs a;
   a.q = q;
@@ -158,14 +155,10 @@ int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
   a.softmax_scale = softmax_scale;
   a.dtype = dtype;
   a.out_dtype = out_dtype;
-  a.workspace = workspace;
-  a.workspace_bytes = workspace_bytes;
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
   return fat::launch_prefill_varlen(a);
 }
-
-size_t fat_prefill_workspace_size(void) { return fat::kPrefillWorkspaceBytes; }
 
 int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_page_bytes, int64_t stride_slot_bytes,
                      int64_t stride_head_bytes, int64_t num_pages, const int32_t* page_table,

@@ -12,14 +12,13 @@
 //               its S row, keeps the running max and sum in registers, writes P
 //               (16-bit) over its S row, and rescales its O row in tensor
 //               memory only when the row max grew by more than 2^8 (P <= 256);
-//   warp 8      work scheduler and TMA producer of Q and K, warp 10 TMA
-//               producer of V (K and V fill independent 128-byte-swizzled
-//               rings, so K runs ahead of V);
+//   warp 8      TMA producer: both Q tiles once, then K and V tiles into two
+//               independent 128-byte-swizzled rings;
 //   warp 9      tcgen05 issuer (one thread), per K/V tile j:
 //                 O0 += P0 V_{j-1};  S0 = Q0 K_j^T;  O1 += P1 V_{j-1};  S1 = Q1 K_j^T
 //               so the tensor core works on one tile while the other tile's
 //               softmax runs (ping-pong between the two warpgroups);
-//   warp 11     idle (it completes the third warpgroup for setmaxnreg).
+//   warps 10-11 idle (they complete the third warpgroup for setmaxnreg).
 // Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D),
 // O1 [384,384+D).  P_t is written over S_t; S_t(j) is issued after O_t += P_t(j-1)
 // V_{j-1} by the same thread, and tcgen05.mma operations of one thread execute
@@ -28,8 +27,6 @@
 // Every wait is bounded; on a timeout the CTA records FAT_DEVERR_TIMEOUT,
 // drains its copies and MMAs, frees tensor memory and exits.
 #include <math_constants.h>
-
-#include <algorithm>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -44,9 +41,8 @@ constexpr int BN = 128;    // keys per K/V tile
 constexpr int kTiles = 2;  // query tiles per CTA
 constexpr int kRowsPerCta = BM * kTiles;
 constexpr int kSoftmaxThreads = 128;  // per tile
-constexpr int kProducerWarp = 8;   // scheduler, Q and K loads
+constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kVProducerWarp = 10;  // V loads
 constexpr int kThreads = 12 * 32;
 constexpr uint32_t kTmemCols = 512;
 // Register split: launched at 168 per thread (65536 / 384, rounded to 8); the
@@ -56,21 +52,17 @@ constexpr int kRegsSoftmax = 208;
 constexpr int kRegsOther = 88;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * 168, "register split exceeds the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 without rescaling
-constexpr int kL2Ahead = 4;                 // K/V tiles requested into L2 ahead of their loads
 
 struct Params {
   const int* cu_q;
   const int* cu_k;
   void* out;
   long long o_st, o_sh;
-  int num_heads, group, batch;
-  int pairs;        // query-tile pairs of the longest sequence
-  int total_items;  // pairs * batch * num_heads
+  int num_heads, group;
   float scale_log2;
   int causal;
   int out_f32;
   int* err;
-  int* sched;  // [0]: next work item, [1]: CTAs finished (zero before and after every launch)
 };
 
 template <int D>
@@ -79,10 +71,8 @@ struct Layout {
   static constexpr int kTile = BM * D * 2;  // one Q, K or V tile
   static constexpr int kStagesK = D <= 64 ? 4 : 3;
   static constexpr int kStagesV = D <= 64 ? 4 : 2;
-  static constexpr int kItemSlots = 2;
-  // q_full, q_empty, K/V rings, s_full/p_full/o_full/o_empty per tile, item ring, drain
-  static constexpr int kBars = 2 + 2 * kStagesK + 2 * kStagesV + 4 * kTiles + 2 * kItemSlots + 1;
-  static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + 8 * kBars + 32;
+  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 2 * kTiles + 1) + 16;
+  static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
   static constexpr uint32_t kColS = 0;    // S_t at column kColS + 128 t
   static constexpr uint32_t kColO = 256;  // O_t at columns [256 + 128 t, 256 + 128 t + D)
 };
@@ -102,7 +92,7 @@ __device__ __forceinline__ void regs_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Regs));
 }
 
-// Number of K/V tiles the query tile starting at row m0 needs (0 if the tile is empty).
+// Number of K/V tiles query tile `t` of the CTA needs (0 if the tile is empty).
 __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int causal) {
   if (m0 >= q_len || kv_len <= 0) return 0;
   const int n_kv = (kv_len + BN - 1) / BN;
@@ -111,41 +101,29 @@ __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int c
   return lim < 0 ? 0 : min(n_kv, lim / BN + 1);
 }
 
-// One work item: a pair of query tiles of one (sequence, head).  Items are
-// numbered heaviest first: item = y * (batch * heads) + b * heads + h with
-// pair = pairs - 1 - y, so every CTA claims the longest remaining work.
-struct Item {
-  int b, h, m0, q0, q_len, k0, kv_len, n0, n1, n_max, q_tiles;
-};
-
-__device__ __forceinline__ Item decode_item(const Params& p, int item) {
-  Item it;
-  const int per_pair = p.batch * p.num_heads;
-  const int y = item / per_pair, x = item - y * per_pair;
-  it.b = x / p.num_heads;
-  it.h = x - it.b * p.num_heads;
-  it.m0 = (p.pairs - 1 - y) * kRowsPerCta;
-  it.q0 = __ldg(p.cu_q + it.b);
-  it.q_len = __ldg(p.cu_q + it.b + 1) - it.q0;
-  it.k0 = __ldg(p.cu_k + it.b);
-  it.kv_len = __ldg(p.cu_k + it.b + 1) - it.k0;
-  it.n0 = tiles_needed(it.m0, it.q_len, it.kv_len, p.causal);
-  it.n1 = tiles_needed(it.m0 + BM, it.q_len, it.kv_len, p.causal);
-  it.n_max = max(it.n0, it.n1);
-  it.q_tiles = (it.m0 + BM < it.q_len) ? 2 : 1;
-  return it;
-}
-
-// Persistent: one CTA per SM claims work items from p.sched[0] until none are left.
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
   using L = Layout<D>;
-  constexpr int SK = L::kStagesK, SV = L::kStagesV, NI = L::kItemSlots;
+  constexpr int SK = L::kStagesK, SV = L::kStagesV;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdescQK = tc::idesc_f16(BM, BN, fmt, 0, 0);
   constexpr uint32_t kIdescPV = tc::idesc_f16(BM, D, fmt, 0, 1);
+
+  const int h = blockIdx.x % p.num_heads;
+  const int b = blockIdx.x / p.num_heads;
+  const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
+  const int q0 = __ldg(p.cu_q + b), q_len = __ldg(p.cu_q + b + 1) - q0;
+  const int k0 = __ldg(p.cu_k + b), kv_len = __ldg(p.cu_k + b + 1) - k0;
+  const int m0 = pair * kRowsPerCta;
+  if (m0 >= q_len) return;  // uniform for the CTA, before any barrier or allocation
+  const int kvh = h / p.group;
+  const int offset = kv_len - q_len;  // bottom-right causal alignment
+  const int n0 = tiles_needed(m0, q_len, kv_len, p.causal);
+  const int n1 = tiles_needed(m0 + BM, q_len, kv_len, p.causal);
+  const int n_max = max(n0, n1);
+  const int q_tiles = (m0 + BM < q_len) ? 2 : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -155,20 +133,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(L::kTile) * (kTiles + SK + SV));
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t q_full = bar0;
-  const uint32_t q_empty = q_full + 8;          // last S MMA of an item done: Q buffers free
-  const uint32_t k_full = q_empty + 8;          // [SK]
-  const uint32_t k_empty = k_full + 8 * SK;     // [SK]
-  const uint32_t v_full = k_empty + 8 * SK;     // [SV]
-  const uint32_t v_empty = v_full + 8 * SV;     // [SV]
-  const uint32_t s_full = v_empty + 8 * SV;     // [kTiles]: S_t(j) complete (and every earlier MMA)
+  const uint32_t k_full = bar0 + 8;          // [SK]
+  const uint32_t k_empty = k_full + 8 * SK;  // [SK]
+  const uint32_t v_full = k_empty + 8 * SK;  // [SV]
+  const uint32_t v_empty = v_full + 8 * SV;  // [SV]
+  const uint32_t s_full = v_empty + 8 * SV;  // [kTiles]: S_t(j) complete (and every earlier MMA)
   const uint32_t p_full = s_full + 8 * kTiles;  // [kTiles]: P_t(j) written, O_t rescaled
-  const uint32_t o_full = p_full + 8 * kTiles;  // [kTiles]: last P.V of an item complete
-  const uint32_t o_empty = o_full + 8 * kTiles; // [kTiles]: O_t read out by the epilogue
-  const uint32_t item_full = o_empty + 8 * kTiles;  // [NI]
-  const uint32_t item_empty = item_full + 8 * NI;   // [NI]
-  const uint32_t drain = item_empty + 8 * NI;
-  volatile int* item_slot = reinterpret_cast<volatile int*>(bars + L::kBars);  // [NI]
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(item_slot + NI);
+  const uint32_t drain = p_full + 8 * kTiles;   // every MMA of the CTA complete
+  volatile uint32_t* tmem_slot =
+      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -178,7 +151,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (tid == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
     for (int s = 0; s < SK; ++s) {
       mbar_init(k_full + 8 * s, 1);
       mbar_init(k_empty + 8 * s, 1);
@@ -190,12 +162,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(s_full + 8 * t, 1);
       mbar_init(p_full + 8 * t, kSoftmaxThreads);
-      mbar_init(o_full + 8 * t, 1);
-      mbar_init(o_empty + 8 * t, kSoftmaxThreads);
-    }
-    for (int s = 0; s < NI; ++s) {
-      mbar_init(item_full + 8 * s, 1);
-      mbar_init(item_empty + 8 * s, 2 + 2 * kSoftmaxThreads);  // MMA, V producer, both softmax warpgroups
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -208,122 +174,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= kProducerWarp) {
     regs_dec<kRegsOther>();
-    if (warp == kProducerWarp && lane == 0) {
-      // ==================== scheduler + TMA producer of Q and K ====================
+    if (warp == kProducerWarp && lane == 0 && n_max > 0) {
+      // ============================ TMA producer ============================
+      int issued_k = 0, issued_v = 0;
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      int kc = 0;       // K tiles loaded so far (ring position)
-      int q_loads = 0;  // items whose Q tiles were loaded
-      // Claims run one item ahead of the loads, so the global atomics are off
-      // the critical path.  An empty item (a pair past its sequence's end)
-      // means every head of that sequence is empty at that pair index: skip
-      // them all with one atomicMax.
-      auto claim = [&]() -> int {
-        while (!*abort_flag) {
-          const int c = atomicAdd(p.sched, 1);
-          if (c >= p.total_items) return -1;
-          const Item it = decode_item(p, c);
-          if (it.m0 < it.q_len) return c;
-          const int next_row = c - it.h + p.num_heads;  // first head of the next sequence
-          atomicMax(p.sched, next_row);
-        }
-        return -1;
-      };
-      int next_item = claim();
-      for (int seq = 0;; ++seq) {
-        int item = next_item;
-        const int slot = seq % NI;
-        if (!mbar_wait_bounded(item_empty + 8 * slot, ((seq / NI) & 1) ^ 1, p.err, abort_flag)) item = -1;
-        item_slot[slot] = item;
-        mbar_arrive(item_full + 8 * slot);
-        if (item < 0) break;
-        const Item it = decode_item(p, item);
-        const int kvh = it.h / p.group;
-        if (it.n_max == 0) {  // nothing to load: the softmax warps write zeros
-          next_item = claim();
-          continue;
-        }
-        // K/V tiles are read by every query tile of the sequence at about the
-        // same time, so the first reader of a tile usually misses L2: request
-        // the item's Q tiles and its K/V tiles kL2Ahead blocks ahead into L2,
-        // so that the shared-memory loads hit.
-        for (int t = 0; t < it.q_tiles; ++t)
+      mbar_arrive_expect_tx(q_full, q_tiles * L::kTile);
+      for (int t = 0; t < q_tiles; ++t)
 #pragma unroll
-          for (int cb = 0; cb < L::kCB; ++cb) tma_prefetch_l2_3d(&tm_q, cb * 64, it.h, it.q0 + it.m0 + t * BM);
-        for (int j = 0; j < min(kL2Ahead, it.n_max); ++j)
+        for (int cb = 0; cb < L::kCB; ++cb)
+          tma_load_3d(sQ + t * L::kTile + cb * BM * 128, &tm_q, q_full, cb * 64, h, q0 + m0 + t * BM);
+      for (int j = 0; j < n_max; ++j) {
+        const int sk = j % SK, sv = j % SV;
+        if (!mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
 #pragma unroll
-          for (int cb = 0; cb < L::kCB; ++cb) {
-            tma_prefetch_l2_3d(&tm_k, cb * 64, kvh, it.k0 + j * BN);
-            tma_prefetch_l2_3d(&tm_v, cb * 64, kvh, it.k0 + j * BN);
-          }
-        // Q tiles: the previous item's last Q.K^T must have finished reading them.
-        if (q_loads > 0 && !mbar_wait_bounded(q_empty, (q_loads - 1) & 1, p.err, abort_flag)) break;
-        ++q_loads;
-        mbar_arrive_expect_tx(q_full, it.q_tiles * L::kTile);
-        for (int t = 0; t < it.q_tiles; ++t)
+        for (int cb = 0; cb < L::kCB; ++cb)
+          tma_load_3d(sK + sk * L::kTile + cb * BN * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, k0 + j * BN);
+        ++issued_k;
+        if (!mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full + 8 * sv, L::kTile);
 #pragma unroll
-          for (int cb = 0; cb < L::kCB; ++cb)
-            tma_load_3d(sQ + t * L::kTile + cb * BM * 128, &tm_q, q_full, cb * 64, it.h, it.q0 + it.m0 + t * BM);
-        bool claimed = false;
-        for (int j = 0; j < it.n_max; ++j) {
-          const int sk = kc % SK;
-          if (j == 1 || (j == 0 && it.n_max == 1)) {
-            next_item = claim();  // while the first tiles load
-            claimed = true;
-          }
-          if (j + kL2Ahead < it.n_max) {
-#pragma unroll
-            for (int cb = 0; cb < L::kCB; ++cb) {
-              tma_prefetch_l2_3d(&tm_k, cb * 64, kvh, it.k0 + (j + kL2Ahead) * BN);
-              tma_prefetch_l2_3d(&tm_v, cb * 64, kvh, it.k0 + (j + kL2Ahead) * BN);
-            }
-          }
-          if (!mbar_wait_bounded(k_empty + 8 * sk, ((kc / SK) & 1) ^ 1, p.err, abort_flag)) break;
-          mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
-#pragma unroll
-          for (int cb = 0; cb < L::kCB; ++cb)
-            tma_load_3d(sK + sk * L::kTile + cb * BN * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, it.k0 + j * BN);
-          ++kc;
-        }
-        if (!claimed) next_item = claim();
-        if (*abort_flag) break;
+        for (int cb = 0; cb < L::kCB; ++cb)
+          tma_load_3d(sV + sv * L::kTile + cb * BN * 128, &tm_v, v_full + 8 * sv, cb * 64, kvh, k0 + j * BN);
+        ++issued_v;
       }
       if (*abort_flag) {
-        // Drain this thread's own copies before the shared memory goes away: the
-        // last completed phase of every stage, waited without the abort flag.
-        if (q_loads > 0) mbar_wait_bounded(q_full, (q_loads - 1) & 1, nullptr, nullptr);
-        for (int c = max(0, kc - SK); c < kc; ++c)
-          mbar_wait_bounded(k_full + 8 * (c % SK), (c / SK) & 1, nullptr, nullptr);
+        // Drain this CTA's own copies before the shared memory goes away.
+        mbar_wait_bounded(q_full, 0, nullptr, nullptr);
+        for (int j = max(0, issued_k - SK); j < issued_k; ++j)
+          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr);
+        for (int j = max(0, issued_v - SV); j < issued_v; ++j)
+          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
       }
-    } else if (warp == kVProducerWarp && lane == 0) {
-      // ============================ TMA producer of V ============================
-      tma_prefetch_desc(&tm_v);
-      int vc = 0;  // V tiles loaded so far
-      for (int seq = 0;; ++seq) {
-        const int slot = seq % NI;
-        if (!mbar_wait_bounded(item_full + 8 * slot, (seq / NI) & 1, p.err, abort_flag)) break;
-        const int item = item_slot[slot];
-        mbar_arrive(item_empty + 8 * slot);
-        if (item < 0) break;
-        const Item it = decode_item(p, item);
-        const int kvh = it.h / p.group;
-        for (int j = 0; j < it.n_max; ++j) {
-          const int sv = vc % SV;
-          if (!mbar_wait_bounded(v_empty + 8 * sv, ((vc / SV) & 1) ^ 1, p.err, abort_flag)) break;
-          mbar_arrive_expect_tx(v_full + 8 * sv, L::kTile);
-#pragma unroll
-          for (int cb = 0; cb < L::kCB; ++cb)
-            tma_load_3d(sV + sv * L::kTile + cb * BN * 128, &tm_v, v_full + 8 * sv, cb * 64, kvh, it.k0 + j * BN);
-          ++vc;
-        }
-        if (*abort_flag) break;
-      }
-      if (*abort_flag) {
-        for (int c = max(0, vc - SV); c < vc; ++c)
-          mbar_wait_bounded(v_full + 8 * (c % SV), (c / SV) & 1, nullptr, nullptr);
-      }
-    } else if (warp == kMmaWarp && lane == 0) {
+    } else if (warp == kMmaWarp && lane == 0 && n_max > 0) {
       // ============================ MMA issuer ============================
       // The issue loop is kept lean (the tensor core retires an M128 N128 K16
       // MMA every 64 cycles, so per-MMA address arithmetic shows up directly
@@ -350,94 +235,57 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::mma_ts(d_tmem, a_tmem + kk * 8, desc(loV + uint32_t((kk * 16 * 128) >> 4), hiV), kIdescPV,
                      kk > 0 ? 1u : acc0);
       };
-      int sk = 0, kph = 0, sv = 0, vph = 0;  // K / V ring positions and phases
-      int items_loaded = 0;
-      int o_uses0 = 0, o_uses1 = 0;  // items whose P.V wrote O_t so far
-      int pph0 = 0, pph1 = 0;        // phases of p_full[t] consumed so far
-      bool ok = true;
-      for (int seq = 0; ok; ++seq) {
-        const int slot = seq % NI;
-        if (!mbar_wait_bounded(item_full + 8 * slot, (seq / NI) & 1, p.err, abort_flag)) break;
-        const int item = item_slot[slot];
-        mbar_arrive(item_empty + 8 * slot);
-        if (item < 0) break;
-        const Item it = decode_item(p, item);
-        const int n0 = it.n0, n1 = it.n1, n_max = it.n_max;
-        if (n_max == 0) continue;
-        if (!mbar_wait_bounded(q_full, items_loaded & 1, p.err, abort_flag)) break;
-        ++items_loaded;
-        for (int j = 0; j <= n_max; ++j) {
-          if (j < n_max && !mbar_wait_bounded(k_full + 8 * sk, kph, p.err, abort_flag)) {
-            ok = false;
+      int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0;
+      bool ok = mbar_wait_bounded(q_full, 0, p.err, abort_flag);
+      for (int j = 0; ok && j <= n_max; ++j) {
+        if (j < n_max && !mbar_wait_bounded(k_full + 8 * sk, kph, p.err, abort_flag)) break;
+        const uint32_t loK = loK0 + uint32_t(sk) * kTileDesc;
+        const uint32_t loV = loV0 + uint32_t(sv) * kTileDesc;
+        bool v_ready = false;
+        // ---- tile 0: O0 += P0 V_{j-1}, then S0 = Q0 K_j^T ----
+        if (j >= 1 && j <= n0) {
+          if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag) ||
+              !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag))
             break;
+          pph0 ^= 1;
+          v_ready = true;
+          tc::fence_after_sync();
+          issue_pv(tmem + L::kColO, tmem + L::kColS, loV, j > 1 ? 1u : 0u);
+        }
+        if (j < n0) {
+          tc::fence_after_sync();
+          issue_s(tmem + L::kColS, loQ0, loK);
+        }
+        // One s_full phase per S0 and one more after the last P.V: the softmax
+        // warps then know O0 is final.
+        if (j <= n0 && (j < n0 || j > 0)) tc::commit(s_full);
+        // ---- tile 1 ----
+        if (j >= 1 && j <= n1) {
+          if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag) ||
+              (!v_ready && !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag)))
+            break;
+          pph1 ^= 1;
+          tc::fence_after_sync();
+          issue_pv(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j > 1 ? 1u : 0u);
+        }
+        if (j < n1) {
+          tc::fence_after_sync();
+          issue_s(tmem + L::kColS + 128, loQ0 + kTileDesc, loK);
+        }
+        if (j <= n1 && (j < n1 || j > 0)) tc::commit(s_full + 8);
+        // ---- release the tiles this iteration consumed ----
+        if (j >= 1) {  // V_{j-1}
+          tc::commit(v_empty + 8 * sv);
+          if (++sv == SV) {
+            sv = 0;
+            vph ^= 1;
           }
-          const uint32_t loK = loK0 + uint32_t(sk) * kTileDesc;
-          const uint32_t loV = loV0 + uint32_t(sv) * kTileDesc;
-          bool v_ready = false;
-          // ---- tile 0: O0 += P0 V_{j-1}, then S0 = Q0 K_j^T ----
-          if (j >= 1 && j <= n0) {
-            if (j == 1 && o_uses0 > 0 && !mbar_wait_bounded(o_empty, (o_uses0 - 1) & 1, p.err, abort_flag)) {
-              ok = false;
-              break;
-            }
-            if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag) ||
-                !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag)) {
-              ok = false;
-              break;
-            }
-            pph0 ^= 1;
-            v_ready = true;
-            tc::fence_after_sync();
-            issue_pv(tmem + L::kColO, tmem + L::kColS, loV, j > 1 ? 1u : 0u);
-            if (j == n0) {
-              tc::commit(o_full);
-              ++o_uses0;
-            }
-          }
-          if (j < n0) {
-            tc::fence_after_sync();
-            issue_s(tmem + L::kColS, loQ0, loK);
-            tc::commit(s_full);
-          }
-          // ---- tile 1 ----
-          if (j >= 1 && j <= n1) {
-            if (j == 1 && o_uses1 > 0 && !mbar_wait_bounded(o_empty + 8, (o_uses1 - 1) & 1, p.err, abort_flag)) {
-              ok = false;
-              break;
-            }
-            if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag) ||
-                (!v_ready && !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag))) {
-              ok = false;
-              break;
-            }
-            pph1 ^= 1;
-            tc::fence_after_sync();
-            issue_pv(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j > 1 ? 1u : 0u);
-            if (j == n1) {
-              tc::commit(o_full + 8);
-              ++o_uses1;
-            }
-          }
-          if (j < n1) {
-            tc::fence_after_sync();
-            issue_s(tmem + L::kColS + 128, loQ0 + kTileDesc, loK);
-            tc::commit(s_full + 8);
-          }
-          // ---- release the tiles this iteration consumed ----
-          if (j >= 1) {  // V_{j-1}
-            tc::commit(v_empty + 8 * sv);
-            if (++sv == SV) {
-              sv = 0;
-              vph ^= 1;
-            }
-          }
-          if (j < n_max) {  // K_j
-            tc::commit(k_empty + 8 * sk);
-            if (++sk == SK) {
-              sk = 0;
-              kph ^= 1;
-            }
-            if (j == n_max - 1) tc::commit(q_empty);  // last Q.K^T of the item issued
+        }
+        if (j < n_max) {  // K_j
+          tc::commit(k_empty + 8 * sk);
+          if (++sk == SK) {
+            sk = 0;
+            kph ^= 1;
           }
         }
       }
@@ -448,154 +296,137 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     regs_inc<kRegsSoftmax>();
     // ============================ softmax warpgroups ============================
-    const int t = warp >> 2;    // query tile of this warpgroup
-    const int row = tid & 127;  // row of the tile = tensor-memory lane
+    const int t = warp >> 2;              // query tile of this warpgroup
+    const int row = tid & 127;            // row of the tile = tensor-memory lane
+    const int n_t = t == 0 ? n0 : n1;
     const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
     const uint32_t colS = L::kColS + 128 * t, colO = L::kColO + 128 * t;
     const uint32_t sbar = s_full + 8 * t, pbar = p_full + 8 * t;
-    int s_seen = 0, o_seen = 0;  // phases of s_full[t] / o_full[t] consumed so far
+    const int q_idx = m0 + t * BM + row;
+    // Last key this row may see (inclusive).
+    const int lim = p.causal ? min(kv_len - 1, q_idx + offset) : kv_len - 1;
+    float m_used = -CUDART_INF_F, l_sum = 0.f;
     bool ok = true;
-    for (int seq = 0; ok; ++seq) {
-      const int slot = seq % NI;
-      if (!mbar_wait_bounded(item_full + 8 * slot, (seq / NI) & 1, p.err, abort_flag)) break;
-      const int item = item_slot[slot];
-      mbar_arrive(item_empty + 8 * slot);
-      if (item < 0) break;
-      const Item it = decode_item(p, item);
-      const int n_t = t == 0 ? it.n0 : it.n1;
-      const int q_idx = it.m0 + t * BM + row;
-      const int offset = it.kv_len - it.q_len;  // bottom-right causal alignment
-      // Last key this row may see (inclusive).
-      const int lim = p.causal ? min(it.kv_len - 1, q_idx + offset) : it.kv_len - 1;
-      float m_used = -CUDART_INF_F, l_sum = 0.f;
-      for (int j = 0; j < n_t; ++j) {
-        if (!mbar_wait_bounded(sbar, s_seen & 1, p.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        ++s_seen;
-        tc::fence_after_sync();
-        float s[BN];
-        {
-          uint32_t r[BN / 32][32];
+    for (int j = 0; j < n_t; ++j) {
+      if (!mbar_wait_bounded(sbar, j & 1, p.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float s[BN];
+      {
+        uint32_t r[BN / 32][32];
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + colS + 32 * c, r[c]);
+        for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + colS + 32 * c, r[c]);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[c][i]);
+      }
+      const int kv0 = j * BN;
+      if (kv0 + BN - 1 > lim) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) s[i] = (kv0 + i <= lim) ? s[i] : -CUDART_INF_F;
+      }
+      float mx;
+      {
+        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+#pragma unroll
+        for (int i = 4; i < BN; i += 8) {
+          a0 = max3(a0, s[i], s[i + 4]);
+          a1 = max3(a1, s[i + 1], s[i + 5]);
+          a2 = max3(a2, s[i + 2], s[i + 6]);
+          a3 = max3(a3, s[i + 3], s[i + 7]);
+        }
+        mx = fmaxf(max3(a0, a1, a2), a3);
+      }
+      mx *= p.scale_log2;
+      float factor = 1.f;
+      bool grow = false;
+      if (mx > m_used + kRescaleThreshold) {
+        factor = (m_used == -CUDART_INF_F) ? 1.f : fast_exp2(m_used - mx);
+        grow = m_used != -CUDART_INF_F;
+        m_used = mx;
+        l_sum *= factor;
+      }
+      if (__any_sync(0xffffffffu, grow)) {
+        // S_t(j) is complete, so O_t holds every earlier P.V: rescale in place.
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::ld32(lane_base + colO + 32 * c, r);
           tc::wait_ld();
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[c][i]);
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tc::st32(lane_base + colO + 32 * c, r);
         }
-        const int kv0 = j * BN;
-        if (kv0 + BN - 1 > lim) {
-#pragma unroll
-          for (int i = 0; i < BN; ++i) s[i] = (kv0 + i <= lim) ? s[i] : -CUDART_INF_F;
-        }
-        float mx;
-        {
-          float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
-#pragma unroll
-          for (int i = 4; i < BN; i += 8) {
-            a0 = max3(a0, s[i], s[i + 4]);
-            a1 = max3(a1, s[i + 1], s[i + 5]);
-            a2 = max3(a2, s[i + 2], s[i + 6]);
-            a3 = max3(a3, s[i + 3], s[i + 7]);
-          }
-          mx = fmaxf(max3(a0, a1, a2), a3);
-        }
-        mx *= p.scale_log2;
-        float factor = 1.f;
-        bool grow = false;
-        if (mx > m_used + kRescaleThreshold) {
-          factor = (m_used == -CUDART_INF_F) ? 1.f : fast_exp2(m_used - mx);
-          grow = m_used != -CUDART_INF_F;
-          m_used = mx;
-          l_sum *= factor;
-        }
-        if (__any_sync(0xffffffffu, grow)) {
-          // S_t(j) is complete, so O_t holds every earlier P.V: rescale in place.
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tc::ld32(lane_base + colO + 32 * c, r);
-            tc::wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tc::st32(lane_base + colO + 32 * c, r);
-          }
-        }
-        const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
-        float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-#pragma unroll
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t packed[32];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = fast_exp2(fmaf(s[64 * c + 2 * i], p.scale_log2, -msub));
-            const float p1 = fast_exp2(fmaf(s[64 * c + 2 * i + 1], p.scale_log2, -msub));
-            const float p2 = fast_exp2(fmaf(s[64 * c + 2 * i + 2], p.scale_log2, -msub));
-            const float p3 = fast_exp2(fmaf(s[64 * c + 2 * i + 3], p.scale_log2, -msub));
-            sum0 += p0;
-            sum1 += p1;
-            sum2 += p2;
-            sum3 += p3;
-            packed[i] = pack2<T>(p0, p1);
-            packed[i + 1] = pack2<T>(p2, p3);
-          }
-          tc::st32(lane_base + colS + 32 * c, packed);
-        }
-        l_sum += (sum0 + sum1) + (sum2 + sum3);
-        tc::wait_st();
-        tc::fence_before_sync();
-        mbar_arrive(pbar);
       }
-      if (!ok) break;
-      const bool store = q_idx < it.q_len;
-      const long long base = (long long)(it.q0 + q_idx) * p.o_st + (long long)it.h * p.o_sh;
-      if (n_t > 0) {
-        // ---- epilogue: O / l -> global once the last P.V of this tile completed ----
-        if (!mbar_wait_bounded(o_full + 8 * t, o_seen & 1, p.err, abort_flag)) break;
-        ++o_seen;
-        tc::fence_after_sync();
-        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-        // Read all of O_t first and hand the columns back, then store.
-        uint32_t o[D / 32][32];
+      const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
+      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) tc::ld32(lane_base + colO + 32 * c, o[c]);
+      for (int c = 0; c < BN / 64; ++c) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = fast_exp2(fmaf(s[64 * c + 2 * i], p.scale_log2, -msub));
+          const float p1 = fast_exp2(fmaf(s[64 * c + 2 * i + 1], p.scale_log2, -msub));
+          const float p2 = fast_exp2(fmaf(s[64 * c + 2 * i + 2], p.scale_log2, -msub));
+          const float p3 = fast_exp2(fmaf(s[64 * c + 2 * i + 3], p.scale_log2, -msub));
+          sum0 += p0;
+          sum1 += p1;
+          sum2 += p2;
+          sum3 += p3;
+          packed[i] = pack2<T>(p0, p1);
+          packed[i + 1] = pack2<T>(p2, p3);
+        }
+        tc::st32(lane_base + colS + 32 * c, packed);
+      }
+      l_sum += (sum0 + sum1) + (sum2 + sum3);
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(pbar);
+    }
+    // ---- epilogue: O / l -> global, once the last P.V of this tile completed ----
+    if (ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag)) {
+      tc::fence_after_sync();
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const bool store = q_idx < q_len;
+      const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tc::ld32(lane_base + colO + 32 * c, r);
         tc::wait_ld();
-        tc::fence_before_sync();
-        mbar_arrive(o_empty + 8 * t);
         if (store) {
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + 32 * c);
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            if (p.out_f32) {
-              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + 32 * c);
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
+                                   __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + base + 32 * c);
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                dst[i] = make_float4(__uint_as_float(o[c][4 * i]) * inv, __uint_as_float(o[c][4 * i + 1]) * inv,
-                                     __uint_as_float(o[c][4 * i + 2]) * inv, __uint_as_float(o[c][4 * i + 3]) * inv);
-            } else {
-              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + base + 32 * c);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                uint4 v;
-                v.x = pack2<T>(__uint_as_float(o[c][8 * i + 0]) * inv, __uint_as_float(o[c][8 * i + 1]) * inv);
-                v.y = pack2<T>(__uint_as_float(o[c][8 * i + 2]) * inv, __uint_as_float(o[c][8 * i + 3]) * inv);
-                v.z = pack2<T>(__uint_as_float(o[c][8 * i + 4]) * inv, __uint_as_float(o[c][8 * i + 5]) * inv);
-                v.w = pack2<T>(__uint_as_float(o[c][8 * i + 6]) * inv, __uint_as_float(o[c][8 * i + 7]) * inv);
-                dst[i] = v;
-              }
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack2<T>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+              v.y = pack2<T>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+              v.z = pack2<T>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+              v.w = pack2<T>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+              dst[i] = v;
             }
           }
         }
-      } else if (store) {
-        // No visible keys (only reachable with invalid causal inputs): zeros.
-        for (int d = 0; d < D; ++d) {
-          if (p.out_f32) {
-            reinterpret_cast<float*>(p.out)[base + d] = 0.f;
-          } else {
-            reinterpret_cast<T*>(p.out)[base + d] = from_float<T>(0.f);
-          }
+      }
+    } else if (n_t == 0 && q_idx < q_len) {
+      // No visible keys (only reachable with invalid causal inputs): zeros.
+      const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
+      for (int d = 0; d < D; ++d) {
+        if (p.out_f32) {
+          reinterpret_cast<float*>(p.out)[base + d] = 0.f;
+        } else {
+          reinterpret_cast<T*>(p.out)[base + d] = from_float<T>(0.f);
         }
       }
     }
@@ -605,14 +436,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
-  if (tid == 0) {
-    // The last CTA to finish leaves the scheduler counters at zero for the next launch.
-    __threadfence();
-    if (atomicAdd(p.sched + 1, 1) == int(gridDim.x) - 1) {
-      atomicExch(p.sched, 0);
-      atomicExch(p.sched + 1, 0);
-    }
-  }
 }
 
 }  // namespace pre
@@ -662,14 +485,8 @@ int launch_t(const PrefillArgs& a) {
   p.causal = a.causal ? 1 : 0;
   p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
   p.err = a.error_word;
-  const long long pairs = (a.max_seqlen_q + pre::kRowsPerCta - 1) / pre::kRowsPerCta;
-  const long long items = pairs * a.batch * a.num_heads;
-  if (items > 0x7fffffffLL) return unsupported("prefill_varlen: too many query tiles");
-  p.batch = a.batch;
-  p.pairs = int(pairs);
-  p.total_items = int(items);
-  p.sched = static_cast<int*>(a.workspace);
-  const unsigned grid = unsigned(std::min<long long>(items, sm_count(current_device())));
+  const int pairs = (a.max_seqlen_q + pre::kRowsPerCta - 1) / pre::kRowsPerCta;
+  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, pre::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill launch", e);
@@ -699,9 +516,7 @@ int launch_prefill_varlen(const PrefillArgs& a) {
   if (!aligned16(a.out) || (a.o_st * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16 ||
       (a.o_sh * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16)
     return unsupported("prefill_varlen: out must be 16-byte aligned with 16-byte-multiple strides");
-  if (a.workspace == nullptr || a.workspace_bytes < kPrefillWorkspaceBytes ||
-      (reinterpret_cast<uintptr_t>(a.workspace) & 7u) != 0)
-    return invalid("prefill_varlen: workspace must be at least fat_prefill_workspace_size() bytes, 8-byte aligned");
+  if (a.max_seqlen_q > 65535 * pre::kRowsPerCta) return unsupported("prefill_varlen: max_seqlen_q too large");
   const bool bf = a.dtype == FAT_DTYPE_BF16;
   switch (a.head_dim) {
     case 64:

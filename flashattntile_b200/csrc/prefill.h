@@ -24,13 +24,9 @@ struct PrefillArgs {
   int causal;
   float softmax_scale;
   int dtype, out_dtype;
-  void* workspace;  // scheduler counters: zero-filled before the first call, left zero by every call
-  size_t workspace_bytes;
   int32_t* error_word;
   cudaStream_t stream;
 };
-
-constexpr size_t kPrefillWorkspaceBytes = 256;
 
 int launch_prefill_varlen(const PrefillArgs& a);
 

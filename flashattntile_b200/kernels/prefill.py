@@ -106,15 +106,12 @@ def launch_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen
         out = torch.empty(q.shape, dtype=out_dtype, device=dev)
     with torch.cuda.device(idx):
         err = _lib.error_word(dev)
-        # Per-stream zero-filled scratch shared with decode (both leave it zero).
-        ws = _lib.workspace(dev, lib.fat_prefill_workspace_size())
         status = lib.fat_prefill_varlen(
             q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
             v.stride(0), v.stride(1), out.data_ptr(), out.stride(0), out.stride(1), cu_seqlens_q.data_ptr(),
             cu_seqlens_k.data_ptr(), cu_seqlens_q.numel() - 1, q.shape[0], k.shape[0], q.shape[1], k.shape[1],
             q.shape[2], int(max_seqlen_q), int(max_seqlen_k), int(bool(causal)), float(softmax_scale),
-            _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[out_dtype], ws.data_ptr(), ws.numel(), err.data_ptr(),
-            _lib.stream_handle(dev))
+            _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[out_dtype], err.data_ptr(), _lib.stream_handle(dev))
     _lib.check(status, "prefill_varlen")
     return out
 

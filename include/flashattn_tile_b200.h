@@ -175,16 +175,7 @@ int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
                        int64_t out_stride_t, int64_t out_stride_h, const int32_t* cu_seqlens_q,
                        const int32_t* cu_seqlens_k, int batch, int64_t total_q, int64_t total_k, int num_heads,
                        int num_kv_heads, int head_dim, int max_seqlen_q, int max_seqlen_k, int causal,
-                       float softmax_scale, int dtype, int out_dtype, void* workspace, size_t workspace_bytes,
-                       int32_t* error_word, void* stream);
-
-/*
- * Bytes of scratch fat_prefill_varlen needs (work-item counters of its persistent
- * grid).  The scratch must be zero-filled before the first call; every call leaves
- * it zero, so calls ordered on one stream may share it (a decode workspace of the
- * same stream may be reused: both leave their scratch zero-filled).
- */
-size_t fat_prefill_workspace_size(void);
+                       float softmax_scale, int dtype, int out_dtype, int32_t* error_word, void* stream);
 
 /*
  * Page-table gather: out_k/out_v [batch, max_len, num_kv_heads, row_bytes] (contiguous)

@@ -61,7 +61,7 @@ def test_host_side_validation_errors_without_gpu():
                               2, 4, 2, 128, 24, 0, 0, 0, 0.1, 1, None, 0, None, None)
     assert rc == _lib.FAT_ERR_UNSUPPORTED and b"page_size" in lib.fat_last_error()
     rc = lib.fat_prefill_varlen(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, None, None, 1, 1, 1, 4, 2, 64, 1, 1,
-                                1, 0.1, 2, 2, None, 0, None, None)
+                                1, 0.1, 2, 2, None, None)
     assert rc == _lib.FAT_ERR_UNSUPPORTED and b"fp16 or bf16" in lib.fat_last_error()
 
 
