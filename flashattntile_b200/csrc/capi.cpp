@@ -60,6 +60,8 @@ int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const vo
   a.kv_dtype = kv_dtype;
   a.out_dtype = out_dtype;
   a.softmax_scale = softmax_scale;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
   a.lse = lse;

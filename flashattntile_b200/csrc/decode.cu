@@ -38,9 +38,7 @@
 namespace fat {
 namespace dec {
 
-constexpr int kWarps = 4;                  // consumer warps
 constexpr int kProducers = 2;              // producer warps (take turns by chunk)
-constexpr int kThreads = (kWarps + kProducers) * 32;
 constexpr int kMaxChunk = 256;             // largest chunk (tokens per pipeline stage) of any layout
 constexpr int kMaxBoxes = 32;              // TMA row boxes per chunk at most (chunk / 8)
 constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
@@ -100,8 +98,13 @@ struct Layout {
   static constexpr int kRowBytes = D * EB;                         // one token row of one KV head
   static constexpr int kBoxBytes = kRowBytes >= 128 ? 128 : kRowBytes;  // TMA box row
   static constexpr int kCB = kRowBytes / kBoxBytes;                // column boxes per row
+  // Consumer warps: 8-bit caches carry twice the tokens per byte and widen
+  // every code before the MMA, so they get twice the math warps.
+  static constexpr int kWarps = (EB == 1 && D <= 128) ? 8 : 4;
+  static constexpr int kThreads = (kWarps + kProducers) * 32;
   // Tokens per consumer warp per stage: stages stay 32 KB (K + V) for narrow rows.
-  static constexpr int kTW = kRowBytes >= 256 ? 16 : (kRowBytes >= 128 ? 32 : 64);
+  static constexpr int kTW = (kRowBytes >= 256 ? 16 : (kRowBytes >= 128 ? 32 : 64)) * 4 / kWarps;
+  static_assert(kTW % 16 == 0, "a consumer warp takes whole 16-token MMA slices");
   static constexpr int kChunk = kWarps * kTW;                      // tokens per pipeline stage
   static_assert(kChunk <= kMaxChunk, "chunk larger than the per-stage metadata");
   static constexpr int kTile = kChunk * kRowBytes;                 // K (or V) bytes per stage
@@ -207,12 +210,19 @@ struct Widen<__nv_bfloat16, FAT_DTYPE_E4M3> {
   }
 };
 
+template <int KVT>
+constexpr int elem_bytes() {
+  return (KVT == FAT_DTYPE_I8 || KVT == FAT_DTYPE_E4M3) ? 1 : 2;
+}
+
 template <typename T, int D, int KVT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const Params p) {
-  constexpr int EB = (KVT == FAT_DTYPE_I8 || KVT == FAT_DTYPE_E4M3) ? 1 : 2;
+  constexpr int EB = elem_bytes<KVT>();
   using L = Layout<D, EB>;
+  constexpr int kWarps = L::kWarps;
+  constexpr int kThreads = L::kThreads;
   constexpr int kStages = L::kStages;
   constexpr int kChunk = L::kChunk;
   constexpr int kTW = L::kTW;
@@ -945,7 +955,7 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   p.lse = a.lse;
   p.lse_sb = a.lse_sb;
   (void)device;
-  kern<<<grid, dec::kThreads, L::kSmem, a.stream>>>(tmk, tmv, p);
+  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tmk, tmv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("paged_decode launch", e);
   return FAT_OK;

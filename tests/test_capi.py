@@ -76,3 +76,27 @@ def test_status_codes_map_to_python_exceptions():
     with pytest.raises(RuntimeError):
         _lib.check(_lib.FAT_ERR_CUDA, "x")
     _lib.check(_lib.FAT_OK, "x")
+
+
+def test_every_decode_entry_forwards_its_scratch_arguments():
+    """With every other pointer present (16-byte aligned dummies, never dereferenced
+    because validation fails first), a NULL or too-small scratch must be rejected
+    by each decode entry point -- proof that the entry forwards what it was given."""
+    import ctypes
+
+    from flashattntile_b200 import _lib
+
+    lib = _lib.load()
+    buf = (ctypes.c_uint8 * 4096)()
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    q = k = v = out = base
+    table = lens = base + 1024
+    lse = base + 2048
+    common = (q, 128 * 4, 128, k, v, 16 * 2 * 128, 2 * 128, 128, 4, table, 2, 2, lens, None, None, 0, out, 4 * 128,
+              128)
+    tail_dims = (2, 4, 2, 128, 16, 0, 0, 0, 0.1, 1)
+    for ws, nbytes, want in ((None, 0, _lib.FAT_ERR_INVALID_ARGUMENT), (base, 16, _lib.FAT_ERR_WORKSPACE)):
+        rc = lib.fat_paged_decode(*common, *tail_dims, ws, nbytes, None, None)
+        assert rc == want, (rc, lib.fat_last_error())
+        rc = lib.fat_paged_decode_lse(*common, lse, 4, *tail_dims, ws, nbytes, None, None)
+        assert rc == want, (rc, lib.fat_last_error())
