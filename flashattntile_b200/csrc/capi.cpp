@@ -6,6 +6,7 @@
 #include "decode.h"
 #include "gather.h"
 #include "merge.h"
+#include "append.h"
 #include "prefill.h"
 #include "host_util.h"
 
@@ -189,6 +190,42 @@ int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_pa
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
   return fat::launch_gather_paged(a);
+}
+
+int fat_append_tokens(void* k_cache, void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot,
+                      int64_t kv_stride_head, int64_t num_pages, const int32_t* page_table, int64_t page_table_stride,
+                      int64_t max_pages, int32_t* seq_lens, const void* new_k, const void* new_v,
+                      int64_t new_stride_b, int64_t new_stride_h, float* k_scale, float* v_scale,
+                      int64_t scale_stride_page, int batch, int num_kv_heads, int head_dim, int page_size,
+                      int kv_dtype, int new_dtype, int32_t* error_word, void* stream) {
+  fat::set_last_error("");
+  fat::AppendArgs a;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.kv_sp = kv_stride_page;
+  a.kv_ss = kv_stride_slot;
+  a.kv_sh = kv_stride_head;
+  a.num_pages = num_pages;
+  a.page_table = page_table;
+  a.pt_sb = page_table_stride;
+  a.max_pages = max_pages;
+  a.seq_lens = seq_lens;
+  a.new_k = new_k;
+  a.new_v = new_v;
+  a.new_sb = new_stride_b;
+  a.new_sh = new_stride_h;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.scale_sp = scale_stride_page;
+  a.batch = batch;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.page_size = page_size;
+  a.kv_dtype = kv_dtype;
+  a.new_dtype = new_dtype;
+  a.error_word = error_word;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return fat::launch_append_tokens(a);
 }
 
 }  // extern "C"

@@ -26,7 +26,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _lib
+from . import _config, _lib
 
 
 @dataclass
@@ -149,8 +149,26 @@ def allocate(batch: int, max_seq_len: int, num_kv_heads: int, head_dim: int, pag
     return cache
 
 
+def _check_append_values(cache: PagedKVCache) -> None:
+    """The reference's value checks of an append (``paging.py:192-203``), read back in one transfer."""
+    positions = cache.seq_lens.long()
+    page_idx = torch.div(positions, cache.page_size, rounding_mode="floor").clamp_max(cache.max_pages_per_seq - 1)
+    rows = torch.arange(cache.batch_size, device=cache.page_table.device)
+    phys = cache.page_table[rows, page_idx.to(cache.page_table.device)].long()
+    pmin, pmax = torch.aminmax(phys)
+    stats = torch.stack([positions.max().to(pmin.device), pmin, pmax]).tolist()
+    _assert(int(stats[0]) < cache.capacity, f"append would exceed page-table capacity {cache.capacity}")
+    _assert(int(stats[1]) >= 0 and int(stats[2]) < cache.num_pages,
+            f"page_table maps to a page outside [0, {cache.num_pages})")
+
+
 def append_tokens(cache: PagedKVCache, new_k: torch.Tensor, new_v: torch.Tensor) -> None:
-    """Append one token per sequence in place (``paging.py:172-210``)."""
+    """Append one token per sequence in place (``paging.py:172-210``), in one CUDA kernel.
+
+    Checks and messages are the reference's; the value checks (capacity, page
+    ids) read ``seq_lens``/``page_table`` back in one transfer when value
+    checks are on, and are otherwise left to the kernel, which skips a bad
+    sequence and records ``FAT_DEVERR_BAD_PAGE`` (``device_error()``)."""
     validate_metadata(cache)
     shape = (cache.batch_size, cache.num_kv_heads, cache.head_dim)
     _assert(new_k.shape == shape, f"new_k must be [{shape[0]}, {shape[1]}, {shape[2]}], got {tuple(new_k.shape)}")
@@ -159,19 +177,13 @@ def append_tokens(cache: PagedKVCache, new_k: torch.Tensor, new_v: torch.Tensor)
     _assert(new_v.dtype == cache.k_cache.dtype, f"new_v dtype {new_v.dtype} != cache dtype {cache.k_cache.dtype}")
     _assert(new_k.device == cache.k_cache.device, "new_k must be on the cache device")
     _assert(new_v.device == cache.k_cache.device, "new_v must be on the cache device")
-    positions = cache.seq_lens.long()
-    _assert(int(positions.max()) < cache.capacity, f"append would exceed page-table capacity {cache.capacity}")
-    page_idx = torch.div(positions, cache.page_size, rounding_mode="floor")
-    rows = torch.arange(cache.batch_size, device=cache.page_table.device)
-    phys = cache.page_table[rows, page_idx.to(cache.page_table.device)].long()
-    pmin, pmax = torch.aminmax(phys)
-    _assert(int(pmin) >= 0 and int(pmax) < cache.num_pages,
-            f"page_table maps to a page outside [0, {cache.num_pages})")
-    phys = phys.to(cache.k_cache.device)
-    slots = (positions % cache.page_size).to(cache.k_cache.device)
-    cache.k_cache[phys, slots] = new_k
-    cache.v_cache[phys, slots] = new_v
-    cache.seq_lens += 1
+    if cache.batch_size == 0:
+        return
+    if _config.validate_values():
+        _check_append_values(cache)
+    from .kernels.append import launch_append
+
+    launch_append(cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, new_k, new_v, cache.page_size)
 
 
 def gather_paged(k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor, seq_lens: torch.Tensor,

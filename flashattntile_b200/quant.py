@@ -132,3 +132,41 @@ def kv_bytes_per_token(num_kv_heads: int, head_dim: int, storage: str = "fp16", 
     """K+V bytes per cached token including the scale overhead (``quant.py:194-208``)."""
     elem = {"fp16": 2, "bf16": 2, "fp32": 4, "int8": 1, "fp8": 1}[storage]
     return float(2 * num_kv_heads * head_dim * elem + 2 * num_kv_heads * 4 / page_size)
+
+
+def append_tokens_quantized(cache: PagedKVCache, scales, new_k: torch.Tensor, new_v: torch.Tensor) -> None:
+    """Append one token per sequence to an INT8 / FP8 cache, quantising on write (one CUDA kernel).
+
+    No reference counterpart: FlashAttnTile appends only to 16-bit caches
+    (``paging.py:172-210``) and quantises whole caches offline
+    (``quant.py:84-142``).  This keeps that offline format exact on the fly:
+    the page receiving a token gets the scale ``quantize_kv_pages`` would give
+    the sequence's tokens on it (earlier ones dequantised as ``code * scale``,
+    plus the new one), earlier codes are requantised when the scale changed,
+    and the new token is quantised with it.  ``new_k``/``new_v`` are
+    ``[batch, num_kv_heads, head_dim]`` fp16 / bf16 / fp32; ``scales`` is a
+    ``QuantScales`` or a dict with ``k``/``v`` (updated in place, like the codes
+    and ``cache.seq_lens``)."""
+    from .kernels.append import launch_append
+    from .paging import _assert, _check_append_values, validate_metadata
+    from . import _config
+
+    validate_metadata(cache)
+    k_scale = scales["k"] if isinstance(scales, dict) else scales.k
+    v_scale = scales["v"] if isinstance(scales, dict) else scales.v
+    quant_dtypes = (torch.int8,) + ((FP8_DTYPE,) if FP8_DTYPE is not None else ())
+    _assert(cache.k_cache.dtype in quant_dtypes, f"expected an int8/float8 cache, got {cache.k_cache.dtype}")
+    shape = (cache.batch_size, cache.num_kv_heads, cache.head_dim)
+    _assert(new_k.shape == shape, f"new_k must be [{shape[0]}, {shape[1]}, {shape[2]}], got {tuple(new_k.shape)}")
+    _assert(new_v.shape == new_k.shape, f"new_v shape {tuple(new_v.shape)} != new_k shape {tuple(new_k.shape)}")
+    _assert(new_k.dtype in (torch.float16, torch.bfloat16, torch.float32) and new_v.dtype == new_k.dtype,
+            f"new_k/new_v must share a float dtype (fp16, bf16, fp32), got {new_k.dtype}/{new_v.dtype}")
+    expected = (cache.num_pages, cache.num_kv_heads)
+    _assert(tuple(k_scale.shape) == expected and tuple(v_scale.shape) == expected,
+            f"scales must have shape {expected}, got {tuple(k_scale.shape)}")
+    if cache.batch_size == 0:
+        return
+    if _config.validate_values():
+        _check_append_values(cache)
+    launch_append(cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, new_k, new_v, cache.page_size,
+                  k_scale=k_scale, v_scale=v_scale)

@@ -21,6 +21,8 @@
  *                             kernels/prefill.py:236-326 (prefill_attention)
  *   fat_gather_paged          flashattn_tile/paging.py:213-256 (gather_paged)
  *   fat_lse_merge             kernels/decode.py:316-356 (_decode_reduce_kernel)
+ *   fat_append_tokens         flashattn_tile/paging.py:172-210 (append_tokens); for 8-bit
+ *                             caches also quant.py:84-142 (per-page scales, applied on write)
  */
 #ifndef FLASHATTN_TILE_B200_H_
 #define FLASHATTN_TILE_B200_H_
@@ -176,6 +178,28 @@ int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
                        const int32_t* cu_seqlens_k, int batch, int64_t total_q, int64_t total_k, int num_heads,
                        int num_kv_heads, int head_dim, int max_seqlen_q, int max_seqlen_k, int causal,
                        float softmax_scale, int dtype, int out_dtype, int32_t* error_word, void* stream);
+
+/*
+ * Append one token per sequence: new_k/new_v [batch, num_kv_heads, head_dim]
+ * (element strides new_stride_b, new_stride_h; unit stride along head_dim) go to
+ * page page_table[b, seq_lens[b] / page_size], slot seq_lens[b] % page_size, then
+ * seq_lens[b] += 1 -- all on the device, no host synchronisation.  A position past
+ * the page table or a page id outside [0, num_pages) leaves that sequence untouched
+ * and ORs FAT_DEVERR_BAD_PAGE into *error_word.
+ *   16-bit caches: new_dtype == kv_dtype, bit-exact copy; k_scale/v_scale unused.
+ *   INT8 / FP8-e4m3 caches: new_dtype F16 | BF16 | F32; the page's fp32 scale
+ *   (k_scale/v_scale [num_pages, num_kv_heads], stride scale_stride_page) becomes
+ *   max(absmax / maxval, 1e-8) over this sequence's tokens on the page (earlier ones
+ *   dequantised as code * scale) and the new token; earlier codes are requantised
+ *   when the scale changed; the new token is quantised with it (int8: round half to
+ *   even, clamp +-127; e4m3: clamp +-448, round to nearest even).
+ */
+int fat_append_tokens(void* k_cache, void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot,
+                      int64_t kv_stride_head, int64_t num_pages, const int32_t* page_table, int64_t page_table_stride,
+                      int64_t max_pages, int32_t* seq_lens, const void* new_k, const void* new_v,
+                      int64_t new_stride_b, int64_t new_stride_h, float* k_scale, float* v_scale,
+                      int64_t scale_stride_page, int batch, int num_kv_heads, int head_dim, int page_size,
+                      int kv_dtype, int new_dtype, int32_t* error_word, void* stream);
 
 /*
  * Page-table gather: out_k/out_v [batch, max_len, num_kv_heads, row_bytes] (contiguous)

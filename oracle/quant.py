@@ -61,6 +61,53 @@ def dequantize_kv_pages(qk, qv, scale_k, scale_v, mode: str):
     return deq(qk, scale_k), deq(qv, scale_v)
 
 
+def append_tokens_quantized(qk, qv, scale_k, scale_v, page_table, seq_lens, new_k, new_v, page_size, mode):
+    """Quantise-on-write append, in place (the semantics of ``fat_append_tokens``
+    for 8-bit caches; no FlashAttnTile counterpart -- it extends
+    ``paging.py:172-210`` to the format of ``quant.py:84-142``).
+
+    For each sequence b, with pos = seq_lens[b], page = page_table[b, pos //
+    page_size], slot = pos % page_size, and per KV head: the new scale is
+    ``max(max(absmax_old, absmax_new) / maxval, 1e-8)`` where ``absmax_old =
+    max|code| * scale`` over slots ``[0, slot)`` (0 when slot == 0); the old codes
+    are requantised from ``code * old_scale`` when the scale changed; the new
+    token is quantised with the new scale.  All arithmetic in float32, one
+    rounding per operation.  ``new_k``/``new_v`` are float32 (the caller widens
+    16-bit inputs exactly).  FP8 codes are uint8 bit patterns."""
+    max_val = np.float32(INT8_MAX if mode == "int8" else FP8_MAX)
+    min_scale = np.float32(MIN_SCALE)
+
+    def decode(c):
+        return c.astype(np.float32) if mode == "int8" else numerics.e4m3_bits_to_f32(c)
+
+    def encode(v):
+        v = np.asarray(v, np.float32)
+        if mode == "int8":
+            return np.clip(np.round(v), -max_val, max_val).astype(np.int8)
+        return numerics.f32_to_e4m3_bits(np.clip(v, -max_val, max_val))
+
+    for b in range(seq_lens.shape[0]):
+        pos = int(seq_lens[b])
+        page = int(page_table[b, pos // page_size])
+        slot = pos % page_size
+        for codes, scales, new in ((qk, scale_k, new_k), (qv, scale_v, new_v)):
+            for h in range(codes.shape[2]):
+                x = np.asarray(new[b, h], np.float32)
+                amax_new = np.float32(np.abs(x).max())
+                s_old = np.float32(scales[page, h])
+                amax_old = np.float32(0.0)
+                if slot > 0:
+                    cmax = np.float32(np.abs(decode(codes[page, :slot, h])).max())
+                    amax_old = np.float32(cmax * s_old)
+                s_new = np.float32(max(np.float32(max(amax_old, amax_new) / max_val), min_scale))
+                if slot > 0 and s_new != s_old:
+                    old = (decode(codes[page, :slot, h]) * s_old).astype(np.float32)
+                    codes[page, :slot, h] = encode(old / s_new)
+                codes[page, slot, h] = encode(x / s_new)
+                scales[page, h] = s_new
+        seq_lens[b] += 1
+
+
 def kv_bytes_per_token(num_kv_heads: int, head_dim: int, storage: str = "fp16", page_size: int = 16) -> float:
     """``kv_bytes_per_token`` (``quant.py:194-208``)."""
     elem = {"fp16": 2, "bf16": 2, "fp32": 4, "int8": 1, "fp8": 1}[storage]
