@@ -198,7 +198,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--only", choices=["decode", "quant", "prefill", "longctx"], default=None,
+    ap.add_argument("--only", choices=["decode", "quant", "prefill", "longctx", "loop"], default=None,
                     help="run one workload (profiling); decode = the headline line without secondary")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -226,7 +226,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     peaks = _peaks()
-    if args.only in ("quant", "prefill", "longctx"):
+    if args.only in ("quant", "prefill", "longctx", "loop"):
         res = run_secondary(device, args, peaks, which=(args.only,), dist=dist)
         if rank == 0:
             print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup, "results": res}),
@@ -290,7 +290,7 @@ def main() -> None:
 
     secondary = {}
     if not args.no_secondary:
-        which = ("quant", "prefill", "longctx") if world == 1 else ("longctx",)
+        which = ("quant", "prefill", "longctx", "loop") if world == 1 else ("longctx",)
         secondary = run_secondary(device, args, peaks, which=which, dist=dist)
     if dist is not None:
         dist.barrier()
@@ -340,9 +340,11 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def run_secondary(device, args, peaks, which=("quant", "prefill", "longctx"), dist=None) -> dict:
-    """Quantised decode (cfg4), varlen prefill (cfg3), long-context decode (cfg5)."""
+def run_secondary(device, args, peaks, which=("quant", "prefill", "longctx", "loop"), dist=None) -> dict:
+    """Quantised decode (cfg4), varlen prefill (cfg3), long-context decode (cfg5), decode loop."""
     res = {}
+    if "loop" in which:
+        res.update(run_decode_loop(device, args))
     if "quant" in which:
         res.update(run_quant(device, args, peaks))
     if "prefill" in which:
@@ -350,6 +352,62 @@ def run_secondary(device, args, peaks, which=("quant", "prefill", "longctx"), di
     if "longctx" in which:
         res.update(run_longctx(device, args, peaks, dist))
     return res
+
+
+def run_decode_loop(device, args) -> dict:
+    """Per-token latency of a serving decode iteration at cfg2 shapes (B32, H32/8,
+    D128, ps16, contexts ~3.8-4k): append the step's K/V, attend, read the output
+    back.  Three ways: the reference's flow (custom op + append_tokens with the
+    default host-side value checks), the same without value checks, and one
+    CUDA-graph replay of both kernels (DecodeLoop).  Host wall time per step,
+    synchronised every step as a sampler would be."""
+    from flashattntile_b200 import value_checks
+    from flashattntile_b200.decode_loop import DecodeLoop
+    from flashattntile_b200.paging import PagedKVCache, append_tokens
+
+    c = CFG2
+    b, h, hkv, d, ps = c["batch"], c["heads"], c["kv_heads"], c["head_dim"], c["page_size"]
+    pages = 4160 // ps
+    gen = torch.Generator(device=device).manual_seed(9)
+    pool = b * pages
+    k = torch.randn((pool, ps, hkv, d), generator=gen, device=device).half()
+    v = torch.randn((pool, ps, hkv, d), generator=gen, device=device).half()
+    table = torch.randperm(pool, generator=gen, device=device).view(b, pages).to(torch.int32)
+    cache = PagedKVCache(k, v, table, torch.full((b,), 3800, dtype=torch.int32, device=device), ps)
+    q = torch.randn((b, h, d), generator=gen, device=device).half()
+    nk = torch.randn((b, hkv, d), generator=gen, device=device).half()
+    nv = torch.randn_like(nk)
+    scale = d ** -0.5
+    n = 50
+
+    def eager():
+        append_tokens(cache, nk, nv)
+        return torch.ops.flashattn_tile.paged_decode(q, cache.k_cache, cache.v_cache, cache.page_table,
+                                                     cache.seq_lens, ps, scale, 1)
+
+    def wall(fn, steps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            out = fn()
+            out.view(-1)[0].item()  # the sampler reads the step's result
+            times.append(time.perf_counter() - t0)
+        return statistics.median(times) * 1e6
+
+    checked = wall(eager, n)
+    with value_checks(False):
+        unchecked = wall(eager, n)
+    loop = DecodeLoop(cache, h)
+    graphed = wall(lambda: loop.step(q, nk, nv), 2 * n)
+    del loop
+    return {"decode_loop_cfg2": {
+        "unit": "us/step (median host wall, synchronised each step)", "batch": b,
+        "reference_flow_us": round(checked, 1), "no_value_checks_us": round(unchecked, 1),
+        "cuda_graph_us": round(graphed, 1), "cuda_graph_tokens_per_s": round(b / (graphed * 1e-6), 1),
+        "step": "append K/V (device kernel) + paged decode; graph = both kernels in one replay"}}
 
 
 CFG5 = dict(batch=8, heads=64, kv_heads=8, head_dim=128, page_size=64, ctx=131072)

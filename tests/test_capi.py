@@ -100,3 +100,15 @@ def test_every_decode_entry_forwards_its_scratch_arguments():
         assert rc == want, (rc, lib.fat_last_error())
         rc = lib.fat_paged_decode_lse(*common, lse, 4, *tail_dims, ws, nbytes, None, None)
         assert rc == want, (rc, lib.fat_last_error())
+
+
+def test_decode_loop_has_no_cpu_path():
+    import torch
+
+    from flashattntile_b200.decode_loop import DecodeLoop
+    from flashattntile_b200.paging import PagedKVCache
+
+    k = torch.zeros(4, 16, 2, 64, dtype=torch.float16)
+    cache = PagedKVCache(k, k.clone(), torch.zeros(1, 4, dtype=torch.int32), torch.zeros(1, dtype=torch.int32), 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        DecodeLoop(cache, num_heads=4)
