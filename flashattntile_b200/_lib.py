@@ -71,6 +71,11 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _i32, _i32,
          _i32, _i32, _i32, _i32, _f32, _i32, _i32, _vp, _vp],
     ),
+    "fat_prefill_paged": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i32, _i64,
+         _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _vp, _vp],
+    ),
     "fat_append_tokens": (
         _i32,
         [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32,

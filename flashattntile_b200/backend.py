@@ -7,6 +7,11 @@ else to ``paged_decode_attention`` (``backend.py:175``), squeezing a
 ``[B, 1, H, D]`` decode query (``backend.py:142-143``).  ``kv_cache`` may also
 be one ``(2, blocks, block_size, kv_heads, head_dim)`` tensor, as a serving
 engine holds it; its K/V halves are then used zero-copy.
+
+Prefill without packed ``k``/``v`` in the metadata (the reference raises,
+``backend.py:158-162``) reads K/V from the paged cache instead: chunked prefill
+and prefix caching, where the new tokens' K/V are already in the cache and
+``seq_lens`` counts every cached token of each sequence.
 """
 
 from __future__ import annotations
@@ -16,7 +21,7 @@ from dataclasses import dataclass
 import torch
 
 from .kernels.decode import paged_decode_attention
-from .kernels.prefill import prefill_attention
+from .kernels.prefill import prefill_attention, prefill_paged_attention
 from .paging import PagedKVCache, allocate
 
 KV_CACHE_NDIM = 4
@@ -104,17 +109,24 @@ class FlashAttnTileBackend:
         if query.shape[1] != self.num_heads:
             raise ValueError(f"query has {query.shape[1]} heads, backend expects {self.num_heads}")
         if attn_metadata.is_prefill:
-            if attn_metadata.cu_seqlens_q is None or attn_metadata.cu_seqlens_k is None:
+            paged = (attn_metadata.k is None or attn_metadata.v is None) and (
+                isinstance(kv_cache, torch.Tensor) or attn_metadata.page_table is not None)
+            if attn_metadata.cu_seqlens_q is None or (attn_metadata.cu_seqlens_k is None and not paged):
                 raise ValueError("prefill routing requires cu_seqlens_q and cu_seqlens_k")
             max_q = attn_metadata.max_seqlen_q
             max_k = attn_metadata.max_seqlen_k
             if max_q is None:
                 max_q = int((attn_metadata.cu_seqlens_q[1:] - attn_metadata.cu_seqlens_q[:-1]).max())
-            if max_k is None:
+            if max_k is None and not paged:
                 max_k = int((attn_metadata.cu_seqlens_k[1:] - attn_metadata.cu_seqlens_k[:-1]).max())
             if attn_metadata.k is None or attn_metadata.v is None:
+                if paged:
+                    # K/V through the page table (the cache already holds the new tokens).
+                    cache = self._resolve_cache(kv_cache, attn_metadata)
+                    return prefill_paged_attention(query, cache, attn_metadata.cu_seqlens_q, int(max_q),
+                                                   causal=True, softmax_scale=attn_metadata.softmax_scale)
                 raise ValueError("prefill routing requires attn_metadata.k and attn_metadata.v "
-                                 "(packed [total_k, num_kv_heads, head_dim])")
+                                 "(packed [total_k, num_kv_heads, head_dim]), or a page table for paged prefill")
             return prefill_attention(query, attn_metadata.k, attn_metadata.v, attn_metadata.cu_seqlens_q,
                                      attn_metadata.cu_seqlens_k, int(max_q), int(max_k), causal=True,
                                      softmax_scale=attn_metadata.softmax_scale)

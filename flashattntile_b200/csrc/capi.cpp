@@ -228,4 +228,46 @@ int fat_append_tokens(void* k_cache, void* v_cache, int64_t kv_stride_page, int6
   return fat::launch_append_tokens(a);
 }
 
+int fat_prefill_paged(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache,
+                      const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                      int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                      const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, void* out, int64_t out_stride_t,
+                      int64_t out_stride_h, int batch, int64_t total_q, int num_heads, int num_kv_heads,
+                      int head_dim, int page_size, int max_seqlen_q, int causal, float softmax_scale, int dtype,
+                      int out_dtype, int32_t* error_word, void* stream) {
+  fat::set_last_error("");
+  fat::PrefillArgs a;
+  a.q = q;
+  a.q_st = q_stride_t;
+  a.q_sh = q_stride_h;
+  a.k = k_cache;
+  a.v = v_cache;
+  a.kv_sp = kv_stride_page;
+  a.kv_ss = kv_stride_slot;
+  a.kv_sh = kv_stride_head;
+  a.num_pages = num_pages;
+  a.page_table = page_table;
+  a.pt_sb = page_table_stride;
+  a.max_pages = max_pages;
+  a.cu_q = cu_seqlens_q;
+  a.seq_lens_k = seq_lens_k;
+  a.out = out;
+  a.o_st = out_stride_t;
+  a.o_sh = out_stride_h;
+  a.batch = batch;
+  a.total_q = total_q;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.page_size = page_size;
+  a.max_seqlen_q = max_seqlen_q;
+  a.causal = causal;
+  a.softmax_scale = softmax_scale;
+  a.dtype = dtype;
+  a.out_dtype = out_dtype;
+  a.error_word = error_word;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return fat::launch_prefill_paged(a);
+}
+
 }  // extern "C"

@@ -55,7 +55,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 without resca
 
 struct Params {
   const int* cu_q;
-  const int* cu_k;
+  const int* cu_k;       // packed K/V: [batch + 1] token offsets
   void* out;
   long long o_st, o_sh;
   int num_heads, group;
@@ -63,6 +63,12 @@ struct Params {
   int causal;
   int out_f32;
   int* err;
+  // Paged K/V (kPaged): sequence b's keys are its seq_lens_k[b] cached tokens.
+  const int* page_table;
+  long long pt_sb;
+  int max_pages, num_pages, page_size;
+  int rows_per_box;      // min(page_size, BN): token rows one TMA box brings from one page
+  const int* seq_lens_k;
 };
 
 template <int D>
@@ -71,7 +77,7 @@ struct Layout {
   static constexpr int kTile = BM * D * 2;  // one Q, K or V tile
   static constexpr int kStagesK = D <= 64 ? 4 : 3;
   static constexpr int kStagesV = D <= 64 ? 4 : 2;
-  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 2 * kTiles + 1) + 16;
+  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 2 * kTiles + 2) + 16;
   static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
   static constexpr uint32_t kColS = 0;    // S_t at column kColS + 128 t
   static constexpr uint32_t kColO = 256;  // O_t at columns [256 + 128 t, 256 + 128 t + D)
@@ -101,7 +107,9 @@ __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int c
   return lim < 0 ? 0 : min(n_kv, lim / BN + 1);
 }
 
-template <typename T, int D>
+// kPaged: K/V come from a paged cache through the page table (4-D maps
+// {head_dim, kv head, slot, page}); otherwise from packed [tokens, heads, dim].
+template <typename T, int D, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -115,7 +123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = blockIdx.x / p.num_heads;
   const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
   const int q0 = __ldg(p.cu_q + b), q_len = __ldg(p.cu_q + b + 1) - q0;
-  const int k0 = __ldg(p.cu_k + b), kv_len = __ldg(p.cu_k + b + 1) - k0;
+  const int k0 = kPaged ? 0 : __ldg(p.cu_k + b);
+  const int kv_len = kPaged ? __ldg(p.seq_lens_k + b) : __ldg(p.cu_k + b + 1) - k0;
   const int m0 = pair * kRowsPerCta;
   if (m0 >= q_len) return;  // uniform for the CTA, before any barrier or allocation
   const int kvh = h / p.group;
@@ -140,8 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t s_full = v_empty + 8 * SV;  // [kTiles]: S_t(j) complete (and every earlier MMA)
   const uint32_t p_full = s_full + 8 * kTiles;  // [kTiles]: P_t(j) written, O_t rescaled
   const uint32_t drain = p_full + 8 * kTiles;   // every MMA of the CTA complete
+  const uint32_t vtail = drain + 8;             // paged: a partly valid V tile landed (before zeroing its tail)
   volatile uint32_t* tmem_slot =
-      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 1);
+      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -164,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(p_full + 8 * t, kSoftmaxThreads);
     }
     mbar_init(drain, 1);
+    mbar_init(vtail, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -174,8 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= kProducerWarp) {
     regs_dec<kRegsOther>();
-    if (warp == kProducerWarp && lane == 0 && n_max > 0) {
-      // ============================ TMA producer ============================
+    if (!kPaged && warp == kProducerWarp && lane == 0 && n_max > 0) {
+      // ======================= TMA producer (packed K/V) =======================
       int issued_k = 0, issued_v = 0;
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -207,6 +218,97 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr);
         for (int j = max(0, issued_v - SV); j < issued_v; ++j)
           mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
+      }
+    } else if (kPaged && warp == kProducerWarp && n_max > 0) {
+      // ======================= TMA producer (paged K/V) ========================
+      // The whole warp: lane l brings token rows [l' * rows_per_box, ...) of
+      // column block cb (l = l' * kCB + cb) of one K or V tile from its page.
+      const int rpb = p.rows_per_box;
+      const int pages_per_tile = BN / rpb;
+      const int i_page = lane / L::kCB, cb = lane - i_page * L::kCB;
+      int issued_k = 0, issued_v = 0, tails = 0;
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        mbar_arrive_expect_tx(q_full, q_tiles * L::kTile);
+        for (int t = 0; t < q_tiles; ++t)
+#pragma unroll
+          for (int c2 = 0; c2 < L::kCB; ++c2)
+            tma_load_3d(sQ + t * L::kTile + c2 * BM * 128, &tm_q, q_full, c2 * 64, h, q0 + m0 + t * BM);
+      }
+      bool ok = true;
+      for (int j = 0; ok && j < n_max; ++j) {
+        const int sk = j % SK, sv = j % SV;
+        const int tok0 = j * BN;
+        const int valid_rows = min(BN, kv_len - tok0);
+        // This lane's page: rows [tok0 + i_page * rpb, + rpb) of the sequence.
+        const int row0 = i_page * rpb;
+        int page = -1, slot0 = 0;
+        if (i_page < pages_per_tile && row0 < valid_rows) {
+          const int tok = tok0 + row0;
+          const int lp = tok / p.page_size;
+          slot0 = tok - lp * p.page_size;
+          if (lp < p.max_pages) page = __ldg(p.page_table + (long long)b * p.pt_sb + lp);
+          if (page < 0 || page >= p.num_pages) {
+            raise_error(p.err, FAT_DEVERR_BAD_PAGE);
+            page = -1;
+          }
+        }
+        const unsigned loaded = __ballot_sync(0xffffffffu, page >= 0 && cb == 0);
+        const uint32_t bytes = uint32_t(__popc(loaded)) * uint32_t(rpb) * 128u * L::kCB;
+        // Rows no copy fills (past the sequence, or on a rejected page) are
+        // zeroed in V so that p = 0 there contributes exactly nothing.
+        const bool tail = valid_rows < BN || __popc(loaded) * rpb < BN;
+        // K tile j.
+        if (lane == 0) ok = mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) mbar_arrive_expect_tx(k_full + 8 * sk, bytes);
+        __syncwarp();
+        if (page >= 0)
+          tma_load_4d(sK + sk * L::kTile + cb * BN * 128 + row0 * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, slot0,
+                      page);
+        ++issued_k;
+        // V tile j.
+        if (lane == 0) ok = mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        const uint32_t vbar = tail ? vtail : v_full + 8 * sv;
+        if (lane == 0) mbar_arrive_expect_tx(vbar, bytes);
+        __syncwarp();
+        if (page >= 0)
+          tma_load_4d(sV + sv * L::kTile + cb * BN * 128 + row0 * 128, &tm_v, vbar, cb * 64, kvh, slot0, page);
+        ++issued_v;
+        if (tail) {
+          ++tails;
+          if (lane == 0) ok = mbar_wait_bounded(vtail, (tails - 1) & 1, p.err, abort_flag);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          // Zero every row no copy filled or that lies past the sequence end
+          // (16-byte stores; the swizzle does not matter for zeros), then
+          // publish the tile to the async proxy.
+          const uint32_t vt = sV + sv * L::kTile;
+          for (int i = lane; i < L::kCB * BN * 8; i += 32) {
+            const int c2 = i / (BN * 8), r = (i / 8) % BN;
+            const bool filled = ((loaded >> ((r / rpb) * L::kCB)) & 1u) != 0;
+            if (!filled || r >= valid_rows) {
+              const uint32_t a = vt + uint32_t(c2 * BN * 128 + r * 128 + (i % 8) * 16);
+              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(v_full + 8 * sv);
+        }
+      }
+      if (*abort_flag && lane == 0) {
+        mbar_wait_bounded(q_full, 0, nullptr, nullptr);
+        for (int j = max(0, issued_k - SK); j < issued_k; ++j)
+          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr);
+        for (int j = max(0, issued_v - SV); j < issued_v; ++j)
+          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
+        if (tails > 0) mbar_wait_bounded(vtail, (tails - 1) & 1, nullptr, nullptr);
       }
     } else if (warp == kMmaWarp && lane == 0 && n_max > 0) {
       // ============================ MMA issuer ============================
@@ -448,7 +550,7 @@ namespace {
 template <typename T, int D>
 int launch_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
-  auto kern = pre::prefill_kernel<T, D>;
+  auto kern = pre::prefill_kernel<T, D, false>;
   static_assert(L::kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill)", e);
@@ -473,7 +575,7 @@ int launch_t(const PrefillArgs& a) {
                       &why))
       return invalid("prefill v: " + why);
   }
-  pre::Params p;
+  pre::Params p{};
   p.cu_q = a.cu_q;
   p.cu_k = a.cu_k;
   p.out = a.out;
@@ -493,9 +595,102 @@ int launch_t(const PrefillArgs& a) {
   return FAT_OK;
 }
 
+template <typename T, int D>
+int launch_paged_t(const PrefillArgs& a) {
+  using L = pre::Layout<D>;
+  auto kern = pre::prefill_kernel<T, D, true>;
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
+  if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill paged)", e);
+  std::string why;
+  CUtensorMap tq, tk, tv;
+  {
+    const uint32_t box[3] = {64u, 1u, uint32_t(pre::BM)};
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.num_heads), uint64_t(a.total_q)};
+    const uint64_t strides[2] = {uint64_t(a.q_sh) * 2, uint64_t(a.q_st) * 2};
+    if (!encode_tiled(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.q, dims, strides, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B, &why))
+      return invalid("prefill q: " + why);
+  }
+  const int rpb = a.page_size < pre::BN ? a.page_size : pre::BN;
+  {
+    // {head_dim, kv head, slot, page}: one box = rpb slots of one head of one page.
+    const uint64_t dims[4] = {uint64_t(D), uint64_t(a.num_kv_heads), uint64_t(a.page_size), uint64_t(a.num_pages)};
+    const uint64_t strides[3] = {uint64_t(a.kv_sh) * 2, uint64_t(a.kv_ss) * 2, uint64_t(a.kv_sp) * 2};
+    const uint32_t box[4] = {64u, 1u, uint32_t(rpb), 1u};
+    if (!encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, a.k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                      &why))
+      return invalid("prefill k_cache: " + why);
+    if (!encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, a.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                      &why))
+      return invalid("prefill v_cache: " + why);
+  }
+  pre::Params p{};
+  p.cu_q = a.cu_q;
+  p.out = a.out;
+  p.o_st = a.o_st;
+  p.o_sh = a.o_sh;
+  p.num_heads = a.num_heads;
+  p.group = a.num_heads / a.num_kv_heads;
+  p.scale_log2 = float(double(a.softmax_scale) * 1.4426950408889634);
+  p.causal = a.causal ? 1 : 0;
+  p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
+  p.err = a.error_word;
+  p.page_table = a.page_table;
+  p.pt_sb = a.pt_sb;
+  p.max_pages = int(a.max_pages);
+  p.num_pages = int(a.num_pages);
+  p.page_size = a.page_size;
+  p.rows_per_box = rpb;
+  p.seq_lens_k = a.seq_lens_k;
+  const int pairs = (a.max_seqlen_q + pre::kRowsPerCta - 1) / pre::kRowsPerCta;
+  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
+  kern<<<grid, pre::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_failure("prefill paged launch", e);
+  return FAT_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+int launch_prefill_paged(const PrefillArgs& a) {
+  if (a.batch < 0 || a.total_q < 0) return invalid("prefill_paged: sizes must be non-negative");
+  if (a.num_heads <= 0 || a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads != 0)
+    return invalid("prefill_paged: num_heads must be a positive multiple of num_kv_heads");
+  if (a.dtype != FAT_DTYPE_F16 && a.dtype != FAT_DTYPE_BF16)
+    return unsupported("prefill_paged: q and the cache must be fp16 or bf16");
+  if (a.out_dtype != a.dtype && a.out_dtype != FAT_DTYPE_F32)
+    return invalid("prefill_paged: out dtype must be the input dtype or fp32");
+  if (a.batch == 0 || a.total_q == 0 || a.max_seqlen_q <= 0) return FAT_OK;
+  if (a.q == nullptr || a.k == nullptr || a.v == nullptr || a.out == nullptr || a.cu_q == nullptr ||
+      a.page_table == nullptr || a.seq_lens_k == nullptr)
+    return invalid("prefill_paged: null pointer argument");
+  if (a.num_pages <= 0 || a.max_pages <= 0) return invalid("prefill_paged: empty cache or page table");
+  // One TMA box per (page, 128-byte column block): a page holds a power of two
+  // of at least 8 token rows below 128, or whole 128-row tiles.
+  const int ps = a.page_size;
+  const bool pow2 = ps > 0 && (ps & (ps - 1)) == 0;
+  if (!((pow2 && ps >= 8 && ps <= pre::BN) || (ps > pre::BN && ps % pre::BN == 0)))
+    return unsupported("prefill_paged: page_size must be a power of two in [8, 128] or a multiple of 128, got " +
+                       std::to_string(ps));
+  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || (a.q_st * 2) % 16 || (a.q_sh * 2) % 16 ||
+      (a.kv_sp * 2) % 16 || (a.kv_ss * 2) % 16 || (a.kv_sh * 2) % 16)
+    return unsupported("prefill_paged: q and the cache must be 16-byte aligned with 16-byte-multiple strides");
+  if (!aligned16(a.out) || (a.o_st * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16 ||
+      (a.o_sh * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16)
+    return unsupported("prefill_paged: out must be 16-byte aligned with 16-byte-multiple strides");
+  if (a.max_seqlen_q > 65535 * pre::kRowsPerCta) return unsupported("prefill_paged: max_seqlen_q too large");
+  const bool bf = a.dtype == FAT_DTYPE_BF16;
+  switch (a.head_dim) {
+    case 64:
+      return bf ? launch_paged_t<__nv_bfloat16, 64>(a) : launch_paged_t<__half, 64>(a);
+    case 128:
+      return bf ? launch_paged_t<__nv_bfloat16, 128>(a) : launch_paged_t<__half, 128>(a);
+    default:
+      return unsupported("prefill_paged: head_dim must be 64 or 128, got " + std::to_string(a.head_dim));
+  }
+}
 
 int launch_prefill_varlen(const PrefillArgs& a) {
   if (a.batch < 0 || a.total_q < 0 || a.total_k < 0) return invalid("prefill_varlen: sizes must be non-negative");

@@ -26,8 +26,17 @@ struct PrefillArgs {
   int dtype{}, out_dtype{};
   int32_t* error_word{};
   cudaStream_t stream{};
+  // Paged K/V (launch_prefill_paged): k / v are the caches [pages, page_size, kv heads, dim].
+  const int32_t* page_table{};
+  int64_t pt_sb{}, max_pages{}, num_pages{};
+  int64_t kv_sp{}, kv_ss{}, kv_sh{};  // element strides: page, slot, head
+  int page_size{};
+  const int32_t* seq_lens_k{};         // [batch] cached tokens per sequence (the keys)
 };
 
 int launch_prefill_varlen(const PrefillArgs& a);
+// Queries of sequence b are its last q_len cached positions (bottom-right
+// causal alignment); keys are its seq_lens_k[b] tokens read through the page table.
+int launch_prefill_paged(const PrefillArgs& a);
 
 }  // namespace fat

@@ -132,3 +132,67 @@ def prefill_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, ma
         raise NotImplementedError(f"prefill has fp16/bf16 kernels only, got {q.dtype}")
     return launch_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q), int(max_seqlen_k), bool(causal),
                           scale)
+
+
+def prefill_paged_attention(q, cache, cu_seqlens_q, max_seqlen_q: int, causal: bool = True,
+                            softmax_scale: float | None = None, out_dtype=None):
+    """Prefill / chunked prefill over a paged cache -> ``[total_q, num_heads, head_dim]``.
+
+    No reference counterpart (FlashAttnTile's prefill needs packed K/V,
+    ``backend.py:158-162``): the keys of sequence b are its ``cache.seq_lens[b]``
+    cached tokens, read through ``cache.page_table``; its ``q_len`` queries (from
+    ``cu_seqlens_q``) are the last ``q_len`` of those positions (bottom-right
+    causal alignment, as ``prefill_attention``).  The new tokens' K/V must
+    already be in the cache (``append_tokens`` or the engine's own writer)."""
+    from ..paging import PagedKVCache, validate_metadata
+
+    if not isinstance(cache, PagedKVCache):
+        raise TypeError("cache must be a PagedKVCache")
+    validate_metadata(cache)
+    if q.dim() != 3 or q.shape[2] != cache.head_dim:
+        raise ValueError(f"q must be [total_q, num_heads, {cache.head_dim}], got {tuple(q.shape)}")
+    if q.shape[1] % cache.num_kv_heads != 0:
+        raise ValueError(f"num_heads {q.shape[1]} must be divisible by num_kv_heads {cache.num_kv_heads}")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_q.dim() != 1 or cu_seqlens_q.numel() != cache.batch_size + 1:
+        raise ValueError("cu_seqlens_q must be int32 [batch + 1]")
+    if q.dtype != cache.k_cache.dtype:
+        raise ValueError(f"q dtype {q.dtype} must match the cache dtype {cache.k_cache.dtype}")
+    for t in (q, cache.k_cache, cache.page_table, cache.seq_lens, cu_seqlens_q):
+        if not t.is_cuda:
+            raise RuntimeError("flashattntile_b200 runs on CUDA tensors only; it has no CPU path")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"prefill has fp16/bf16 kernels only, got {q.dtype}")
+    if max_seqlen_q <= 0:
+        raise ValueError(f"max_seqlen_q must be positive, got {max_seqlen_q}")
+    if _config.validate_values() and cache.batch_size:
+        q_lens = (cu_seqlens_q[1:] - cu_seqlens_q[:-1]).to(cache.seq_lens.device)
+        lo, hi, over = torch.stack([q_lens.min(), q_lens.max(), (q_lens - cache.seq_lens).max()]).tolist()
+        if lo < 0 or hi > max_seqlen_q:
+            raise ValueError(f"q lengths must lie in [0, max_seqlen_q={max_seqlen_q}]")
+        if causal and over > 0:
+            raise ValueError("causal paged prefill needs q_len <= cached length for every sequence")
+        from ..paging import validate_cache
+
+        validate_cache(cache)
+    scale = float(softmax_scale) if softmax_scale is not None else q.shape[-1] ** -0.5
+    if cache.k_cache.stride() != cache.v_cache.stride() or cache.k_cache.stride(3) != 1:
+        raise ValueError("k_cache and v_cache need equal strides and a contiguous head_dim")
+    page_table = cache.page_table if cache.page_table.stride(1) == 1 else cache.page_table.contiguous()
+    dev = q.device
+    out_dtype = out_dtype or q.dtype
+    out = torch.empty(q.shape, dtype=out_dtype, device=dev)
+    if q.stride(2) != 1 or (q.stride(0) * q.element_size()) % 16 or (q.stride(1) * q.element_size()) % 16:
+        q = q.contiguous()
+    lib = _lib.load()
+    k = cache.k_cache
+    with torch.cuda.device(dev):
+        err = _lib.error_word(dev)
+        status = lib.fat_prefill_paged(
+            q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), cache.v_cache.data_ptr(), k.stride(0), k.stride(1),
+            k.stride(2), k.shape[0], page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+            cu_seqlens_q.contiguous().data_ptr(), cache.seq_lens.contiguous().data_ptr(), out.data_ptr(),
+            out.stride(0), out.stride(1), cache.batch_size, q.shape[0], q.shape[1], cache.num_kv_heads,
+            cache.head_dim, cache.page_size, int(max_seqlen_q), int(bool(causal)), scale,
+            _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[out_dtype], err.data_ptr(), _lib.stream_handle(dev))
+    _lib.check(status, "prefill_paged")
+    return out

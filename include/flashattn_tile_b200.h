@@ -21,6 +21,9 @@
  *                             kernels/prefill.py:236-326 (prefill_attention)
  *   fat_gather_paged          flashattn_tile/paging.py:213-256 (gather_paged)
  *   fat_lse_merge             kernels/decode.py:316-356 (_decode_reduce_kernel)
+ *   fat_prefill_paged         no counterpart: prefill (kernels/prefill.py:34-138 semantics) with
+ *                             K/V read through the page table instead of packed tensors
+ *                             (the reference's backend requires packed K/V, backend.py:158-162)
  *   fat_append_tokens         flashattn_tile/paging.py:172-210 (append_tokens); for 8-bit
  *                             caches also quant.py:84-142 (per-page scales, applied on write)
  */
@@ -178,6 +181,25 @@ int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
                        const int32_t* cu_seqlens_k, int batch, int64_t total_q, int64_t total_k, int num_heads,
                        int num_kv_heads, int head_dim, int max_seqlen_q, int max_seqlen_k, int causal,
                        float softmax_scale, int dtype, int out_dtype, int32_t* error_word, void* stream);
+
+/*
+ * Prefill / chunked prefill over a paged cache: sequence b has q_len =
+ * cu_seqlens_q[b+1] - cu_seqlens_q[b] queries (packed q, as fat_prefill_varlen)
+ * that are the last q_len of its seq_lens_k[b] cached tokens; keys and values
+ * are those tokens, read from k_cache/v_cache [num_pages, page_size, num_kv_heads,
+ * head_dim] through page_table [batch, max_pages] (bottom-right causal alignment:
+ * query i sees key j <= i + seq_lens_k[b] - q_len).  fp16/bf16; head_dim 64 or 128;
+ * page_size a power of two in [8, 128] or a multiple of 128.  Rows past a
+ * sequence's end never contribute; a page id outside [0, num_pages) is skipped
+ * and ORs FAT_DEVERR_BAD_PAGE into *error_word.
+ */
+int fat_prefill_paged(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache,
+                      const void* v_cache, int64_t kv_stride_page, int64_t kv_stride_slot, int64_t kv_stride_head,
+                      int64_t num_pages, const int32_t* page_table, int64_t page_table_stride, int64_t max_pages,
+                      const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, void* out, int64_t out_stride_t,
+                      int64_t out_stride_h, int batch, int64_t total_q, int num_heads, int num_kv_heads,
+                      int head_dim, int page_size, int max_seqlen_q, int causal, float softmax_scale, int dtype,
+                      int out_dtype, int32_t* error_word, void* stream);
 
 /*
  * Append one token per sequence: new_k/new_v [batch, num_kv_heads, head_dim]
