@@ -565,6 +565,42 @@ def run_prefill(device, args, peaks) -> dict:
             "frac_tensor": round(tflops / peaks["bf16_tflops"], 4),
             "peak_source": "measured cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops)"}
         del sets
+    # The same cfg3 prefill with K/V read through a page table (ps 16, permuted pages).
+    from flashattntile_b200.kernels.prefill import prefill_paged_attention
+    from flashattntile_b200.paging import PagedKVCache
+
+    ps = 16
+    pages = [n // ps for n in lens]
+    pool = sum(pages)
+    table = torch.zeros((len(lens), max(pages)), dtype=torch.int32, device=device)
+    perm = torch.randperm(pool, generator=g3, device=device).to(torch.int32)
+    off = 0
+    for i, n in enumerate(pages):
+        table[i, :n] = perm[off:off + n]
+        off += n
+    caches = []
+    for _ in range(2):
+        kc = torch.randn((pool, ps, 8, 128), generator=g3, device=device).half()
+        vc = torch.randn((pool, ps, 8, 128), generator=g3, device=device).half()
+        q3 = torch.randn((sum(lens), 32, 128), generator=g3, device=device).half()
+        caches.append((q3, PagedKVCache(kc, vc, table, torch.tensor(lens, dtype=torch.int32, device=device), ps)))
+    state = {"i": 0}
+
+    def ppstep():
+        q3, cache = caches[state["i"] & 1]
+        state["i"] += 1
+        prefill_paged_attention(q3, cache, cu, 4096, causal=True)
+
+    from flashattntile_b200._config import value_checks
+
+    with value_checks(False):
+        times = time_steps(ppstep, max(10, args.steps // 2), args.warmup, None)
+    ms = statistics.mean(times)
+    tflops = flops / (ms * 1e-3) / 1e12
+    res["cfg3_prefill_paged_f16_ps16"] = {
+        "value": round(tflops, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "algorithmic_flops": flops,
+        "frac_tensor": round(tflops / peaks["bf16_tflops"], 4), "page_size": ps}
+    del caches
     torch.cuda.empty_cache()
     return res
 
