@@ -147,3 +147,31 @@ def test_backend_routes_prefill_without_packed_kv_to_pages():
     torch.cuda.synchronize()
     want = _oracle(q, k, v, table, lens, cu_q, 16, torch.float16)
     assert_parity_16bit(out, want, torch.float16)
+
+
+def test_backend_decode_and_packed_prefill_routing():
+    """``backend.forward`` decode (3-D and [B, 1, H, D] queries) and packed prefill
+    equal the oracle (``tests/test_ops.py:111-143`` of the reference, on the GPU)."""
+    from flashattntile_b200.backend import AttentionMetadata, FlashAttnTileBackend
+    from flashattntile_b200.paging import PagedKVCache
+    from tests.helpers import paged_case, varlen_case
+
+    backend = FlashAttnTileBackend(num_heads=8, num_kv_heads=2, head_dim=128, page_size=16)
+    q, k, v, table, lens = paged_case(31, [5, 40, 129], 8, 2, 128, 16, torch.float16)
+    cache = PagedKVCache(k.to(DEV), v.to(DEV), table.to(DEV), lens.to(DEV), 16)
+    md = AttentionMetadata(page_table=cache.page_table, seq_lens=cache.seq_lens, softmax_scale=0.35)
+    out = backend.forward(q.to(DEV), cache, md)
+    out4 = backend.forward(q.to(DEV).unsqueeze(1), cache, md)
+    torch.cuda.synchronize()
+    want = oatt.attention_paged(to_np(q), to_np(k), to_np(v), to_np(table), to_np(lens), 16, scale=0.35, dtype="f16")
+    assert_parity_16bit(out, want, torch.float16)
+    assert torch.equal(out, out4)
+
+    qp, kp, vp, cu_q, cu_k = varlen_case(32, [3, 70], [3, 70], 8, 2, 128, torch.float16)
+    mdp = AttentionMetadata(cu_seqlens_q=cu_q.to(DEV), cu_seqlens_k=cu_k.to(DEV), is_prefill=True, max_seqlen_q=70,
+                            max_seqlen_k=70, k=kp.to(DEV), v=vp.to(DEV), softmax_scale=0.35)
+    outp = backend.forward(qp.to(DEV), cache, mdp)
+    torch.cuda.synchronize()
+    wantp = oatt.attention_varlen(to_np(qp), to_np(kp), to_np(vp), to_np(cu_q), to_np(cu_k), causal=True, scale=0.35,
+                                  dtype="f16")
+    assert_parity_16bit(outp, wantp, torch.float16)
