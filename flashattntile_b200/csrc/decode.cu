@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   long long* shl = reinterpret_cast<long long*>(const_cast<int*>(shi) + 4);   // [0] start_b [1] start_S [2] total
   long long* scan = shl + 4;                                                    // [kThreads]
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(scan + kThreads) + 15) & ~uintptr_t(15));     // producer prefetch ring
+      (reinterpret_cast<uintptr_t>(scan + kThreads + kThreads / 32) + 15) & ~uintptr_t(15));  // producer prefetch ring
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -270,17 +270,29 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     const int b1 = min(p.batch, b0 + per);
     long long mine = 0;
     for (int b = b0; b < b1; ++b) mine += (max(__ldg(p.seq_lens + b), 0) + kChunk - 1) / kChunk;
-    scan[tid] = mine;
-    __syncthreads();
-    if (tid == 0) {
-      long long run = 0;
-      for (int t = 0; t < kThreads; ++t) {
-        long long v = scan[t];
-        scan[t] = run;
-        run += v;
-      }
-      shl[2] = run;
+    // Exclusive prefix sum of `mine` over the block: warp scans, then a scan
+    // of the warp totals by warp 0 (a serial loop here cost microseconds).
+    long long* wsum = scan + kThreads;  // [kThreads / 32]
+    long long v = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
     }
+    if (lane == 31) wsum[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      long long w = lane < kThreads / 32 ? wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      if (lane < kThreads / 32) wsum[lane] = w;  // inclusive totals
+      if (lane == kThreads / 32 - 1) shl[2] = w;
+    }
+    __syncthreads();
+    scan[tid] = v - mine + (warp > 0 ? wsum[warp - 1] : 0);
     __syncthreads();
     const long long total = shl[2] * nkg;
     const long long x0 = range_start(blockIdx.x, total, gridDim.x);
@@ -477,6 +489,26 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
             mt.vscale[lane] = vg;
           }
         }
+        // The copies go out first (their bytes are expected before any can
+        // land); the query rows and the stage metadata are written meanwhile,
+        // and the producer's arrival after them publishes the stage.
+        const uint32_t bytes = uint32_t(__popc(okmask)) * uint32_t(p.box_rows) * uint32_t(L::kRowBytes) * 2u;
+        const uint32_t fb = full0 + 8u * s;
+        if (lane == 0) mbar_expect_tx(fb, bytes);
+        __syncwarp();
+        // One TMA copy per (row box, K|V): the box spans every 128-byte column
+        // block of its rows (5-D map), landing as [rows][row bytes] in the stage.
+        const uint32_t st = smem_u32(stages) + uint32_t(s) * L::kStage;
+        for (int j0 = 0; j0 < 2 * nbox; j0 += 32) {
+          const int j = j0 + lane;
+          const int box = j >> 1, tensor = j & 1;
+          const int ph = __shfl_sync(0xffffffffu, phys, box & 31);
+          if (j < 2 * nbox && ph >= 0) {
+            const int t = tok0 + box * p.box_rows;
+            const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(box * p.box_rows * L::kRowBytes);
+            tma_load_5d(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph);
+          }
+        }
         if (first) {
           // Query rows of this head group -> qarea[s] (zero rows past the group).
           const int rows = min(kRows, p.group - hg * kRows);
@@ -503,23 +535,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
           mt.unit_base = S * nkg + (long long)unit_local * chunks_b;
         }
         __syncwarp();
-        const uint32_t bytes = uint32_t(__popc(okmask)) * uint32_t(p.box_rows) * uint32_t(L::kRowBytes) * 2u;
-        const uint32_t fb = full0 + 8u * s;
-        if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
-        __syncwarp();
-        // One TMA copy per (row box, K|V): the box spans every 128-byte column
-        // block of its rows (5-D map), landing as [rows][row bytes] in the stage.
-        const uint32_t st = smem_u32(stages) + uint32_t(s) * L::kStage;
-        for (int j0 = 0; j0 < 2 * nbox; j0 += 32) {
-          const int j = j0 + lane;
-          const int box = j >> 1, tensor = j & 1;
-          const int ph = __shfl_sync(0xffffffffu, phys, box & 31);
-          if (j < 2 * nbox && ph >= 0) {
-            const int t = tok0 + box * p.box_rows;
-            const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(box * p.box_rows * L::kRowBytes);
-            tma_load_5d(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph);
-          }
-        }
+        if (lane == 0) mbar_arrive(fb);
         ++own_issued;
       }
     }
