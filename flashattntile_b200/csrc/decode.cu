@@ -10,7 +10,9 @@
 //   owns a contiguous range of chunks, so the split adapts to ragged batches.
 //   A unit split across CTAs is merged by a log-sum-exp combine done by the
 //   last CTA that finishes a piece of it (an atomic ticket per unit); the
-//   math is decode.py:12-14 / 341-352 in base 2.
+//   math is decode.py:12-14 / 341-352 in base 2.  A dedicated merge warp
+//   does each piece's global epilogue (output rows, or the partial, ticket
+//   and combine), so its L2 round trips overlap the next chunks' math.
 // * Two producer warps take turns by chunk: each walks the CTA's chunks,
 //   prefetches page ids (and 8-bit scales) through a cp.async ring, and issues
 //   one 5-D TMA copy per (row box, K|V) -- whole token rows of one KV head,
@@ -71,6 +73,16 @@ struct Meta {
   float vscale[kMaxChunk / 8];
 };
 
+// A finished piece, handed from the consumer warps to the merge warp.
+struct MergeEvent {
+  int flags;
+  int b;
+  int unit_local;
+  int chunks_b;
+  long long unit_base;
+  long long pad;
+};
+
 struct Params {
   const void* q;
   long long q_sb, q_sh;
@@ -101,7 +113,8 @@ struct Layout {
   // Consumer warps: 8-bit caches carry twice the tokens per byte and widen
   // every code before the MMA, so they get twice the math warps.
   static constexpr int kWarps = (EB == 1 && D <= 128) ? 8 : 4;
-  static constexpr int kThreads = (kWarps + kProducers) * 32;
+  static constexpr int kMergeWarp = kWarps + kProducers;           // warp index of the merge warp
+  static constexpr int kThreads = (kWarps + kProducers + 1) * 32;
   // Tokens per consumer warp per stage: stages stay 32 KB (K + V) for narrow rows.
   static constexpr int kTW = (kRowBytes >= 256 ? 16 : (kRowBytes >= 128 ? 32 : 64)) * 4 / kWarps;
   static_assert(kTW % 16 == 0, "a consumer warp takes whole 16-token MMA slices");
@@ -114,7 +127,7 @@ struct Layout {
   static constexpr int kMergeFloats = kWarps * kRows * (D + 8) + 2 * kWarps * kRows;
   static constexpr size_t kSmem = 1024 /*align slack*/ + size_t(kStages) * kStage + size_t(kStages) * kQBytes +
                                   size_t(kStages) * sizeof(Meta) + size_t(kMergeFloats) * 4 +
-                                  size_t(2 * kStages + 1) * 8 + 64 + size_t(kThreads) * 16 +
+                                  size_t(2 * kStages + 2) * 8 + 64 + sizeof(MergeEvent) + size_t(kThreads) * 16 +
                                   size_t(kProducers) * kRingBytes + 16;
 
   // Shared address of byte column `bc` (16-byte aligned part) of token row `row`
@@ -136,14 +149,6 @@ __device__ __forceinline__ long long owner_of(long long x, long long total, int 
 }
 
 __device__ __forceinline__ long long range_start(long long c, long long total, int nc) { return c * total / nc; }
-
-// Consumer-group barrier (128 threads) on an mbarrier so that every wait is bounded.
-__device__ __forceinline__ bool consumer_sync(uint32_t bar, int& phase, int* err, volatile int* abort) {
-  mbar_arrive(bar);
-  bool ok = mbar_wait_bounded(bar, uint32_t(phase), err, abort);
-  phase ^= 1;
-  return ok;
-}
 
 // ---------------------------------------------------------------------------
 // 8-bit KV codes -> 16-bit MMA operands, exactly (every int8 and every finite
@@ -237,9 +242,10 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   float* mM = mO + kWarps * kRows * (D + 8);
   float* mL = mM + kWarps * kRows;
   uint64_t* bars = reinterpret_cast<uint64_t*>(mL + kWarps * kRows);
-  volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 1);  // [0] abort [1] last-flag
+  volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 2);  // [0] abort
   long long* shl = reinterpret_cast<long long*>(const_cast<int*>(shi) + 4);   // [0] start_b [1] start_S [2] total
-  long long* scan = shl + 4;                                                    // [kThreads]
+  volatile MergeEvent* evt = reinterpret_cast<volatile MergeEvent*>(shl + 4);
+  long long* scan = reinterpret_cast<long long*>(const_cast<MergeEvent*>(evt) + 1);  // [kThreads]
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(scan + kThreads + kThreads / 32) + 15) & ~uintptr_t(15));  // producer prefetch ring
 
@@ -248,7 +254,8 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   const int lane = tid & 31;
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = full0 + 8u * kStages;
-  const uint32_t csync = full0 + 16u * kStages;
+  const uint32_t mfull = full0 + 16u * kStages;  // consumer warps -> merge warp: a piece is in the merge area
+  const uint32_t mfree = mfull + 8u;             // merge warp -> consumer warps: the merge area is free
   const int nkg = p.num_kv_heads * p.head_groups;
 
   if (tid == 0) {
@@ -256,9 +263,9 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       mbar_init(full0 + 8u * s, 1);
       mbar_init(empty0 + 8u * s, kWarps);
     }
-    mbar_init(csync, kWarps * 32);
+    mbar_init(mfull, kWarps * 32);
+    mbar_init(mfree, 1);
     shi[0] = 0;
-    shi[1] = 0;
     shl[0] = -1;
     fence_barrier_init();
   }
@@ -331,7 +338,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     }
   }
 
-  if (warp >= kWarps) {
+  if (warp >= kWarps && warp < L::kMergeWarp) {
     // ======================= producer warps =======================
     // kProducers warps take turns: producer `pid` fills the stages of chunks
     // pid, pid + kProducers, ... of this CTA's range, so the per-chunk
@@ -561,6 +568,195 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     return;
   }
 
+  if (warp == L::kMergeWarp) {
+    // ======================= merge warp =======================
+    // For each finished piece: fold the consumer warps' partials (merge area)
+    // into registers, free the area, then write the output rows of a unit
+    // this CTA covered whole -- or, for a unit split across CTAs, write the
+    // piece's partial (o, m, l) to its workspace slot and, if it is the last
+    // piece to arrive, combine all pieces of the unit in CTA order (the same
+    // arithmetic whichever CTA arrives last, so results are deterministic).
+    constexpr int VE = D / 32;                 // output columns per lane: d = j * 32 + lane
+    constexpr int kPair = (D <= 128 && EB == 2) ? 2 : 1;  // workspace pieces loaded per round trip
+    const auto store_rows = [&](int b, int h0, int rows, const float (&M)[kRows], const float (&Ls)[kRows],
+                                const float (&O)[kRows][VE]) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        if (r >= rows) break;
+        const long long off = (long long)b * p.o_sb + (long long)(h0 + r) * p.o_sh + lane;
+#pragma unroll
+        for (int j = 0; j < VE; ++j) {
+          const float val = O[r][j] / Ls[r];
+          if (p.out_f32) {
+            reinterpret_cast<float*>(p.out)[off + j * 32] = val;
+          } else {
+            reinterpret_cast<T*>(p.out)[off + j * 32] = from_float<T>(val);
+          }
+        }
+        if (p.lse != nullptr && lane == 0) p.lse[(long long)b * p.lse_sb + h0 + r] = M[r] + __log2f(Ls[r]);
+      }
+    };
+    int ev = 0;
+    while (true) {
+      if (!mbar_wait_bounded(mfull, uint32_t(ev & 1), p.err, abort_flag)) break;
+      const int flags = evt->flags;
+      if (flags & kDone) break;
+      const int b = evt->b, unit_local = evt->unit_local, chunks_b = evt->chunks_b;
+      const long long unit_base = evt->unit_base;
+      const int kvh = unit_local / p.head_groups;
+      const int hg = unit_local - kvh * p.head_groups;
+      const int rows = min(kRows, p.group - hg * kRows);
+      const int h0 = kvh * p.group + hg * kRows;
+
+      float pm[kRows], pl[kRows], po[kRows][VE];
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        pm[r] = -CUDART_INF_F;
+        pl[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < VE; ++j) po[r][j] = 0.f;
+        if (r < rows) {
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) pm[r] = fmaxf(pm[r], mM[w * kRows + r]);
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) {
+            const float wt = fast_exp2(mM[w * kRows + r] - pm[r]);
+            pl[r] += mL[w * kRows + r] * wt;
+#pragma unroll
+            for (int j = 0; j < VE; ++j) po[r][j] += mO[(w * kRows + r) * (D + 8) + j * 32 + lane] * wt;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mfree);
+      ++ev;
+
+      if (flags & kFull) {
+        store_rows(b, h0, rows, pm, pl, po);
+        continue;
+      }
+
+      // ---- a unit split across CTAs ----
+      // Its pieces belong to the CTAs whose (non-empty) chunk ranges overlap
+      // it: owner(first chunk) .. owner(last chunk), skipping CTAs with empty
+      // ranges (more CTAs than chunks when the problem is small).
+      const long long unit = (long long)b * nkg + unit_local;
+      const int ca = int(owner_of(unit_base, total, gridDim.x));
+      const int cb = int(owner_of(unit_base + chunks_b - 1, total, gridDim.x));
+      int parts = 0;
+      for (int cc = ca + lane; cc <= cb; cc += 32)
+        parts += range_start(cc + 1, total, gridDim.x) > range_start(cc, total, gridDim.x) ? 1 : 0;
+      parts = __reduce_add_sync(0xffffffffu, parts);
+      {
+        const long long base = ((long long)blockIdx.x * 2 + ((x0 < unit_base) ? 1 : 0)) * kRows;
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          if (r >= rows) break;
+#pragma unroll
+          for (int j = 0; j < VE; ++j) __stcg(p.ws_o + (base + r) * D + j * 32 + lane, po[r][j]);
+          if (lane == 0) {
+            __stcg(p.ws_ml + (base + r) * 2, pm[r]);
+            __stcg(p.ws_ml + (base + r) * 2 + 1, pl[r]);
+          }
+        }
+      }
+      __syncwarp();
+      // Last piece?  Either every other piece has already taken its ticket
+      // (then this one takes none), or this one's ticket is the last.
+      bool last = ld_acquire_gpu(p.ws_count + unit) == parts - 1;
+      if (!last) {
+        int t = 0;
+        if (lane == 0) {
+          __threadfence();
+          t = atomicAdd(p.ws_count + unit, 1);
+        }
+        last = __shfl_sync(0xffffffffu, t, 0) == parts - 1;
+        if (!last) continue;
+        ld_acquire_gpu(p.ws_count + unit);  // every lane acquires the other pieces' writes
+      }
+
+      float M[kRows], Ls[kRows], O[kRows][VE];
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        M[r] = -CUDART_INF_F;
+        Ls[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < VE; ++j) O[r][j] = 0.f;
+      }
+      // Fold one piece (m, l, o) into the running (M, Ls, O).
+      const auto fold = [&](const float (&qm)[kRows], const float (&ql)[kRows], const float (&qo)[kRows][VE]) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          if (r >= rows) break;
+          const float mn = fmaxf(M[r], qm[r]);
+          const float a = fast_exp2(M[r] - mn);
+          const float w = fast_exp2(qm[r] - mn);
+          Ls[r] = Ls[r] * a + ql[r] * w;
+#pragma unroll
+          for (int j = 0; j < VE; ++j) O[r][j] = O[r][j] * a + qo[r][j] * w;
+          M[r] = mn;
+        }
+      };
+      // Load one piece from its workspace slot and zero the o entries this lane read.
+      const auto load = [&](long long base, float (&qm)[kRows], float (&ql)[kRows], float (&qo)[kRows][VE]) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          if (r >= rows) break;
+          qm[r] = __ldcg(p.ws_ml + (base + r) * 2);
+          ql[r] = __ldcg(p.ws_ml + (base + r) * 2 + 1);
+#pragma unroll
+          for (int j = 0; j < VE; ++j) {
+            qo[r][j] = __ldcg(p.ws_o + (base + r) * D + j * 32 + lane);
+            __stcg(p.ws_o + (base + r) * D + j * 32 + lane, 0.f);
+          }
+        }
+      };
+      for (int c0 = ca; c0 <= cb; c0 += 32) {
+        const int cl = c0 + lane;
+        const long long rs = range_start(cl, total, gridDim.x);
+        const bool has = cl <= cb && range_start(cl + 1, total, gridDim.x) > rs;
+        const long long my_base = ((long long)cl * 2 + ((rs < unit_base) ? 1 : 0)) * kRows;
+        unsigned mask = __ballot_sync(0xffffffffu, has);
+        while (mask != 0u) {
+          const int i0 = __ffs(mask) - 1;
+          mask &= mask - 1u;
+          const long long b0 = __shfl_sync(0xffffffffu, my_base, i0);
+          float am[kRows], al[kRows], ao[kRows][VE];
+          if constexpr (kPair == 2) {
+            if (mask != 0u) {
+              const int i1 = __ffs(mask) - 1;
+              mask &= mask - 1u;
+              const long long b1 = __shfl_sync(0xffffffffu, my_base, i1);
+              float bm[kRows], bl[kRows], bo[kRows][VE];
+              load(b0, am, al, ao);
+              load(b1, bm, bl, bo);
+              fold(am, al, ao);
+              fold(bm, bl, bo);
+              continue;
+            }
+          }
+          load(b0, am, al, ao);
+          fold(am, al, ao);
+        }
+      }
+      store_rows(b, h0, rows, M, Ls, O);
+      // Leave the workspace zero-filled for the next call: the (m, l) pairs
+      // once every lane has read them, then the ticket.
+      __syncwarp();
+      for (int cc = ca + lane; cc <= cb; cc += 32) {
+        const long long rs = range_start(cc, total, gridDim.x);
+        if (range_start(cc + 1, total, gridDim.x) == rs) continue;
+        const long long base = ((long long)cc * 2 + ((rs < unit_base) ? 1 : 0)) * kRows;
+        for (int r = 0; r < rows; ++r) {
+          __stcg(p.ws_ml + (base + r) * 2, 0.f);
+          __stcg(p.ws_ml + (base + r) * 2 + 1, 0.f);
+        }
+      }
+      if (lane == 0) p.ws_count[unit] = 0;
+    }
+    return;
+  }
+
   // ======================= consumer warps =======================
   const int g = lane >> 2;
   const int c = lane & 3;
@@ -569,7 +765,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   float m_run = -CUDART_INF_F, l_run = 0.f;
   uint32_t qa[D / 16][2];
   int it = 0;
-  int cphase = 0;
+  int ev = 0;  // pieces handed to the merge warp
 
   while (true) {
     const int s = it % kStages;
@@ -758,7 +954,9 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     ++it;
 
     if (flags & kLast) {
-      // ---- end of this CTA's piece of a unit: merge the 4 warps ----
+      // ---- end of this CTA's piece of a unit: hand the warps' partials to
+      // the merge warp (once it has taken the previous piece) and go on ----
+      if (ev > 0 && !mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag)) break;
       const float l_row = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
       const float l_tot = l_row + __shfl_xor_sync(0xffffffffu, l_row, 2);
       float* myO = mO + (warp * kRows + g) * (D + 8);
@@ -775,110 +973,22 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         mM[warp * kRows + g] = m_run;
         mL[warp * kRows + g] = l_tot;
       }
-      if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
-
-      const int kvh = unit_local / p.head_groups;
-      const int hg = unit_local - kvh * p.head_groups;
-      const int rows = min(kRows, p.group - hg * kRows);
-      const int h0 = kvh * p.group + hg * kRows;
-      const bool full = (flags & kFull) != 0;
-      const int slot = (x0 < unit_base) ? 1 : 0;
-      for (int idx = ctid; idx < rows * D; idx += kWarps * 32) {
-        const int gg = idx / D, d = idx - gg * D;
-        float M = -CUDART_INF_F;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mM[w * kRows + gg]);
-        float Lsum = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-          const float wt = fast_exp2(mM[w * kRows + gg] - M);
-          Lsum += mL[w * kRows + gg] * wt;
-          O += mO[(w * kRows + gg) * (D + 8) + d] * wt;
-        }
-        if (full) {
-          const long long off = (long long)b * p.o_sb + (long long)(h0 + gg) * p.o_sh + d;
-          const float val = O / Lsum;
-          if (p.out_f32) {
-            reinterpret_cast<float*>(p.out)[off] = val;
-          } else {
-            reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
-          }
-          if (p.lse != nullptr && d == 0) p.lse[(long long)b * p.lse_sb + h0 + gg] = M + __log2f(Lsum);
-        } else {
-          const long long base = ((long long)blockIdx.x * 2 + slot) * kRows + gg;
-          p.ws_o[base * D + d] = O;
-          if (d == 0) {
-            p.ws_ml[base * 2] = M;
-            p.ws_ml[base * 2 + 1] = Lsum;
-          }
-        }
+      if (ctid == 0) {
+        evt->flags = flags;
+        evt->b = b;
+        evt->unit_local = unit_local;
+        evt->chunks_b = chunks_b;
+        evt->unit_base = unit_base;
       }
-      if (!full) {
-        __threadfence();
-        if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
-        const long long unit = (long long)b * nkg + unit_local;
-        // The pieces of this unit belong to the CTAs whose (non-empty) chunk
-        // ranges overlap it: owner(first chunk) .. owner(last chunk), skipping
-        // CTAs with empty ranges (there are more CTAs than chunks when the
-        // problem is small).
-        const int ca = int(owner_of(unit_base, total, gridDim.x));
-        const int cb = int(owner_of(unit_base + chunks_b - 1, total, gridDim.x));
-        if (ctid == 0) {
-          int parts = 0;
-          for (int cc = ca; cc <= cb; ++cc)
-            parts += range_start(cc + 1, total, gridDim.x) > range_start(cc, total, gridDim.x) ? 1 : 0;
-          const int ticket = atomicAdd(p.ws_count + unit, 1);
-          shi[1] = (ticket == parts - 1) ? 1 : 0;
-        }
-        if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
-        if (shi[1]) {
-          __threadfence();
-          for (int idx = ctid; idx < rows * D; idx += kWarps * 32) {
-            const int gg = idx / D, d = idx - gg * D;
-            float M = -CUDART_INF_F;
-            for (int cc = ca; cc <= cb; ++cc) {
-              const long long rs = range_start(cc, total, gridDim.x);
-              if (range_start(cc + 1, total, gridDim.x) == rs) continue;
-              const int sl = (rs < unit_base) ? 1 : 0;
-              M = fmaxf(M, __ldcg(p.ws_ml + (((long long)cc * 2 + sl) * kRows + gg) * 2));
-            }
-            float Lsum = 0.f, O = 0.f;
-            for (int cc = ca; cc <= cb; ++cc) {
-              const long long rs = range_start(cc, total, gridDim.x);
-              if (range_start(cc + 1, total, gridDim.x) == rs) continue;
-              const int sl = (rs < unit_base) ? 1 : 0;
-              const long long base = ((long long)cc * 2 + sl) * kRows + gg;
-              const float wt = fast_exp2(__ldcg(p.ws_ml + base * 2) - M);
-              Lsum += __ldcg(p.ws_ml + base * 2 + 1) * wt;
-              O += __ldcg(p.ws_o + base * D + d) * wt;
-              __stcg(p.ws_o + base * D + d, 0.f);  // only this thread reads this entry
-            }
-            const long long off = (long long)b * p.o_sb + (long long)(h0 + gg) * p.o_sh + d;
-            const float val = O / Lsum;
-            if (p.out_f32) {
-              reinterpret_cast<float*>(p.out)[off] = val;
-            } else {
-              reinterpret_cast<T*>(p.out)[off] = from_float<T>(val);
-            }
-            if (p.lse != nullptr && d == 0) p.lse[(long long)b * p.lse_sb + h0 + gg] = M + __log2f(Lsum);
-          }
-          // Leave the whole workspace zero-filled for the next call, whatever
-          // its shape: the (m, l) pairs once every thread has read them, then
-          // the ticket.
-          if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
-          for (int cc = ca + ctid / kRows; cc <= cb; cc += (kWarps * 32) / kRows) {
-            const int gg = ctid % kRows;
-            const long long rs = range_start(cc, total, gridDim.x);
-            if (gg >= rows || range_start(cc + 1, total, gridDim.x) == rs) continue;
-            const long long base = ((long long)cc * 2 + ((rs < unit_base) ? 1 : 0)) * kRows + gg;
-            __stcg(p.ws_ml + base * 2, 0.f);
-            __stcg(p.ws_ml + base * 2 + 1, 0.f);
-          }
-          if (ctid == 0) p.ws_count[unit] = 0;
-        }
-      }
-      if (!consumer_sync(csync, cphase, p.err, abort_flag)) break;
+      mbar_arrive(mfull);
+      ++ev;
     }
+  }
+  // No more pieces: tell the merge warp (after it has taken the last one).
+  // After an abort it stops on the shared abort flag instead.
+  if (!*abort_flag && (ev == 0 || mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag))) {
+    if (ctid == 0) evt->flags = kDone;
+    mbar_arrive(mfull);
   }
 }
 
