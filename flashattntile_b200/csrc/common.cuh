@@ -34,6 +34,13 @@ __device__ __forceinline__ void raise_error(int* err, int code) {
   if (err != nullptr) atomicOr(err, code);
 }
 
+// GPU-scope acquire load (pairs with a fence + atomic release by another CTA).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Shared-memory addresses and mbarriers
 // ---------------------------------------------------------------------------
@@ -60,12 +67,6 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 }
 
 // Raise the transaction count of the current phase without arriving.
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }

@@ -144,11 +144,25 @@ struct Layout {
   }
 };
 
-__device__ __forceinline__ long long owner_of(long long x, long long total, int nc) {
-  return ((x + 1) * nc - 1) / total;
-}
-
 __device__ __forceinline__ long long range_start(long long c, long long total, int nc) { return c * total / nc; }
+
+// The balanced split of `total` chunks over `nc` CTAs: CTA c owns
+// [start(c), start(c + 1)) and chunk x belongs to owner(x).  32-bit
+// arithmetic whenever the products fit (64-bit division is emulated).
+struct Split {
+  long long total;
+  int nc;
+  bool narrow;
+  __device__ Split(long long t, int n) : total(t), nc(n), narrow((t + 1) * (n + 32) < (1ll << 32)) {}
+  // c <= nc + 31
+  __device__ __forceinline__ long long start(int c) const {
+    return narrow ? (long long)(uint32_t(c) * uint32_t(total) / uint32_t(nc)) : (long long)c * total / nc;
+  }
+  // 0 <= x < total
+  __device__ __forceinline__ int owner(long long x) const {
+    return narrow ? int((uint32_t(x + 1) * uint32_t(nc) - 1u) / uint32_t(total)) : int(((x + 1) * nc - 1) / total);
+  }
+};
 
 // ---------------------------------------------------------------------------
 // 8-bit KV codes -> 16-bit MMA operands, exactly (every int8 and every finite
@@ -584,9 +598,10 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       for (int r = 0; r < kRows; ++r) {
         if (r >= rows) break;
         const long long off = (long long)b * p.o_sb + (long long)(h0 + r) * p.o_sh + lane;
+        const float inv = __frcp_rn(Ls[r]);
 #pragma unroll
         for (int j = 0; j < VE; ++j) {
-          const float val = O[r][j] / Ls[r];
+          const float val = O[r][j] * inv;
           if (p.out_f32) {
             reinterpret_cast<float*>(p.out)[off + j * 32] = val;
           } else {
@@ -596,6 +611,43 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         if (p.lse != nullptr && lane == 0) p.lse[(long long)b * p.lse_sb + h0 + r] = M[r] + __log2f(Ls[r]);
       }
     };
+    // Fold one piece (m, l, o) into the running (M, Ls, O); the first piece is taken as it is.
+    const auto fold = [&](float (&M)[kRows], float (&Ls)[kRows], float (&O)[kRows][VE], int rows,
+                          const float (&qm)[kRows], const float (&ql)[kRows], const float (&qo)[kRows][VE]) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        if (r >= rows) break;
+        if (M[r] == -CUDART_INF_F) {
+          M[r] = qm[r];
+          Ls[r] = ql[r];
+#pragma unroll
+          for (int j = 0; j < VE; ++j) O[r][j] = qo[r][j];
+        } else {
+          const float mn = fmaxf(M[r], qm[r]);
+          const float a = fast_exp2(M[r] - mn);
+          const float w = fast_exp2(qm[r] - mn);
+          Ls[r] = Ls[r] * a + ql[r] * w;
+#pragma unroll
+          for (int j = 0; j < VE; ++j) O[r][j] = O[r][j] * a + qo[r][j] * w;
+          M[r] = mn;
+        }
+      }
+    };
+    // Load one piece from its workspace slot and zero the o entries this lane read.
+    const auto load = [&](long long base, int rows, float (&qm)[kRows], float (&ql)[kRows], float (&qo)[kRows][VE]) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        if (r >= rows) break;
+        qm[r] = __ldcg(p.ws_ml + (base + r) * 2);
+        ql[r] = __ldcg(p.ws_ml + (base + r) * 2 + 1);
+#pragma unroll
+        for (int j = 0; j < VE; ++j) {
+          qo[r][j] = __ldcg(p.ws_o + (base + r) * D + j * 32 + lane);
+          __stcg(p.ws_o + (base + r) * D + j * 32 + lane, 0.f);
+        }
+      }
+    };
+    const Split split(total, gridDim.x);
     int ev = 0;
     while (true) {
       if (!mbar_wait_bounded(mfull, uint32_t(ev & 1), p.err, abort_flag)) break;
@@ -603,27 +655,34 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       if (flags & kDone) break;
       const int b = evt->b, unit_local = evt->unit_local, chunks_b = evt->chunks_b;
       const long long unit_base = evt->unit_base;
+      const bool whole = (flags & kFull) != 0;
+      const long long unit = (long long)b * nkg + unit_local;
+      // A split unit's ticket, read now so that its latency overlaps the fold
+      // below.  An acquire load: if it shows every other piece's ticket, their
+      // workspace writes are visible to this lane (a fence here costs ~1 us).
+      const int ticket0 = whole ? 0 : ld_acquire_gpu(p.ws_count + unit);
       const int kvh = unit_local / p.head_groups;
       const int hg = unit_local - kvh * p.head_groups;
       const int rows = min(kRows, p.group - hg * kRows);
       const int h0 = kvh * p.group + hg * kRows;
 
-      float pm[kRows], pl[kRows], po[kRows][VE];
+      // This piece: the consumer warps' partials folded together.
+      float M[kRows], Ls[kRows], O[kRows][VE];
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
-        pm[r] = -CUDART_INF_F;
-        pl[r] = 0.f;
+        M[r] = -CUDART_INF_F;
+        Ls[r] = 0.f;
 #pragma unroll
-        for (int j = 0; j < VE; ++j) po[r][j] = 0.f;
+        for (int j = 0; j < VE; ++j) O[r][j] = 0.f;
         if (r < rows) {
 #pragma unroll
-          for (int w = 0; w < kWarps; ++w) pm[r] = fmaxf(pm[r], mM[w * kRows + r]);
+          for (int w = 0; w < kWarps; ++w) M[r] = fmaxf(M[r], mM[w * kRows + r]);
 #pragma unroll
           for (int w = 0; w < kWarps; ++w) {
-            const float wt = fast_exp2(mM[w * kRows + r] - pm[r]);
-            pl[r] += mL[w * kRows + r] * wt;
+            const float wt = fast_exp2(mM[w * kRows + r] - M[r]);
+            Ls[r] += mL[w * kRows + r] * wt;
 #pragma unroll
-            for (int j = 0; j < VE; ++j) po[r][j] += mO[(w * kRows + r) * (D + 8) + j * 32 + lane] * wt;
+            for (int j = 0; j < VE; ++j) O[r][j] += mO[(w * kRows + r) * (D + 8) + j * 32 + lane] * wt;
           }
         }
       }
@@ -631,39 +690,48 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       if (lane == 0) mbar_arrive(mfree);
       ++ev;
 
-      if (flags & kFull) {
-        store_rows(b, h0, rows, pm, pl, po);
+      if (whole) {
+        store_rows(b, h0, rows, M, Ls, O);
         continue;
       }
 
       // ---- a unit split across CTAs ----
       // Its pieces belong to the CTAs whose (non-empty) chunk ranges overlap
       // it: owner(first chunk) .. owner(last chunk), skipping CTAs with empty
-      // ranges (more CTAs than chunks when the problem is small).
-      const long long unit = (long long)b * nkg + unit_local;
-      const int ca = int(owner_of(unit_base, total, gridDim.x));
-      const int cb = int(owner_of(unit_base + chunks_b - 1, total, gridDim.x));
+      // ranges (more CTAs than chunks when the problem is small).  A piece's
+      // workspace slot is 1 if it ends its CTA's range, else 0.
+      const int ca = split.owner(unit_base);
+      const int cb = split.owner(unit_base + chunks_b - 1);
+      const auto piece = [&](int cc, long long& base) -> bool {
+        const long long rs = split.start(cc);
+        base = ((long long)cc * 2 + ((rs < unit_base) ? 1 : 0)) * kRows;
+        return cc <= cb && split.start(cc + 1) > rs;
+      };
       int parts = 0;
-      for (int cc = ca + lane; cc <= cb; cc += 32)
-        parts += range_start(cc + 1, total, gridDim.x) > range_start(cc, total, gridDim.x) ? 1 : 0;
-      parts = __reduce_add_sync(0xffffffffu, parts);
-      {
+      for (int c0 = ca; c0 <= cb; c0 += 32) {
+        long long unused;
+        parts += __popc(__ballot_sync(0xffffffffu, piece(c0 + lane, unused)));
+      }
+      // Last piece?  Either every other piece had taken its ticket when this
+      // one looked (then it takes none), or its own ticket is the last one.
+      // The first piece of a unit that arrives last keeps its partial in
+      // registers: it is the first term of the combine either way.
+      bool last = ticket0 == parts - 1;
+      const bool keep = last && ca == int(blockIdx.x);
+      if (!keep) {
         const long long base = ((long long)blockIdx.x * 2 + ((x0 < unit_base) ? 1 : 0)) * kRows;
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
           if (r >= rows) break;
 #pragma unroll
-          for (int j = 0; j < VE; ++j) __stcg(p.ws_o + (base + r) * D + j * 32 + lane, po[r][j]);
+          for (int j = 0; j < VE; ++j) __stcg(p.ws_o + (base + r) * D + j * 32 + lane, O[r][j]);
           if (lane == 0) {
-            __stcg(p.ws_ml + (base + r) * 2, pm[r]);
-            __stcg(p.ws_ml + (base + r) * 2 + 1, pl[r]);
+            __stcg(p.ws_ml + (base + r) * 2, M[r]);
+            __stcg(p.ws_ml + (base + r) * 2 + 1, Ls[r]);
           }
         }
+        __syncwarp();
       }
-      __syncwarp();
-      // Last piece?  Either every other piece has already taken its ticket
-      // (then this one takes none), or this one's ticket is the last.
-      bool last = ld_acquire_gpu(p.ws_count + unit) == parts - 1;
       if (!last) {
         int t = 0;
         if (lane == 0) {
@@ -675,48 +743,15 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         ld_acquire_gpu(p.ws_count + unit);  // every lane acquires the other pieces' writes
       }
 
-      float M[kRows], Ls[kRows], O[kRows][VE];
+      // Combine the pieces in CTA order (the same arithmetic whoever merges).
+      if (!keep) {
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) {
-        M[r] = -CUDART_INF_F;
-        Ls[r] = 0.f;
-#pragma unroll
-        for (int j = 0; j < VE; ++j) O[r][j] = 0.f;
+        for (int r = 0; r < kRows; ++r) M[r] = -CUDART_INF_F;
       }
-      // Fold one piece (m, l, o) into the running (M, Ls, O).
-      const auto fold = [&](const float (&qm)[kRows], const float (&ql)[kRows], const float (&qo)[kRows][VE]) {
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-          if (r >= rows) break;
-          const float mn = fmaxf(M[r], qm[r]);
-          const float a = fast_exp2(M[r] - mn);
-          const float w = fast_exp2(qm[r] - mn);
-          Ls[r] = Ls[r] * a + ql[r] * w;
-#pragma unroll
-          for (int j = 0; j < VE; ++j) O[r][j] = O[r][j] * a + qo[r][j] * w;
-          M[r] = mn;
-        }
-      };
-      // Load one piece from its workspace slot and zero the o entries this lane read.
-      const auto load = [&](long long base, float (&qm)[kRows], float (&ql)[kRows], float (&qo)[kRows][VE]) {
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-          if (r >= rows) break;
-          qm[r] = __ldcg(p.ws_ml + (base + r) * 2);
-          ql[r] = __ldcg(p.ws_ml + (base + r) * 2 + 1);
-#pragma unroll
-          for (int j = 0; j < VE; ++j) {
-            qo[r][j] = __ldcg(p.ws_o + (base + r) * D + j * 32 + lane);
-            __stcg(p.ws_o + (base + r) * D + j * 32 + lane, 0.f);
-          }
-        }
-      };
       for (int c0 = ca; c0 <= cb; c0 += 32) {
-        const int cl = c0 + lane;
-        const long long rs = range_start(cl, total, gridDim.x);
-        const bool has = cl <= cb && range_start(cl + 1, total, gridDim.x) > rs;
-        const long long my_base = ((long long)cl * 2 + ((rs < unit_base) ? 1 : 0)) * kRows;
-        unsigned mask = __ballot_sync(0xffffffffu, has);
+        long long my_base;
+        unsigned mask = __ballot_sync(0xffffffffu, piece(c0 + lane, my_base));
+        if (keep && c0 == ca) mask &= ~1u;  // this CTA's piece, already the first term
         while (mask != 0u) {
           const int i0 = __ffs(mask) - 1;
           mask &= mask - 1u;
@@ -728,25 +763,25 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
               mask &= mask - 1u;
               const long long b1 = __shfl_sync(0xffffffffu, my_base, i1);
               float bm[kRows], bl[kRows], bo[kRows][VE];
-              load(b0, am, al, ao);
-              load(b1, bm, bl, bo);
-              fold(am, al, ao);
-              fold(bm, bl, bo);
+              load(b0, rows, am, al, ao);
+              load(b1, rows, bm, bl, bo);
+              fold(M, Ls, O, rows, am, al, ao);
+              fold(M, Ls, O, rows, bm, bl, bo);
               continue;
             }
           }
-          load(b0, am, al, ao);
-          fold(am, al, ao);
+          load(b0, rows, am, al, ao);
+          fold(M, Ls, O, rows, am, al, ao);
         }
       }
       store_rows(b, h0, rows, M, Ls, O);
       // Leave the workspace zero-filled for the next call: the (m, l) pairs
       // once every lane has read them, then the ticket.
       __syncwarp();
-      for (int cc = ca + lane; cc <= cb; cc += 32) {
-        const long long rs = range_start(cc, total, gridDim.x);
-        if (range_start(cc + 1, total, gridDim.x) == rs) continue;
-        const long long base = ((long long)cc * 2 + ((rs < unit_base) ? 1 : 0)) * kRows;
+      for (int c0 = ca; c0 <= cb; c0 += 32) {
+        long long base;
+        const int cc = c0 + lane;
+        if (!piece(cc, base) || (keep && cc == int(blockIdx.x))) continue;
         for (int r = 0; r < rows; ++r) {
           __stcg(p.ws_ml + (base + r) * 2, 0.f);
           __stcg(p.ws_ml + (base + r) * 2 + 1, 0.f);
