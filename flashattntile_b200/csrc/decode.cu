@@ -33,6 +33,8 @@
 // FAT_DEVERR_TIMEOUT, drains its own TMA copies and returns.
 #include <math_constants.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "decode.h"
 #include "host_util.h"
@@ -229,6 +231,28 @@ struct Widen<__nv_bfloat16, FAT_DTYPE_E4M3> {
   }
 };
 
+// int8 codes -> fp16 with a +1152 bias, for fp16 queries: the fp16 bit
+// pattern 0x6400 | (x + 128) is exactly 1152 + x, so dropping the subtraction
+// of the exact widening leaves the byte placement only.  The bias comes back
+// out per row: 1152 * sum(q) from every score and 1152 * sum(p) from every
+// output column (both sums taken in fp32 as the MMAs see their operands).
+constexpr float kI8Bias = 1152.f;
+
+// Bytes 0-3 of w -> biased pairs (b0, b1) and (b2, b3).
+__device__ __forceinline__ void widen_i8_biased(uint32_t w, uint32_t& p01, uint32_t& p23) {
+  const uint32_t u = w ^ 0x80808080u;
+  p01 = __byte_perm(u, 0x64646464u, 0x4140);
+  p23 = __byte_perm(u, 0x64646464u, 0x4342);
+}
+
+// Bytes 0 and 2 of x -> the biased pair (b0, b2): (x & 0x00FF00FF) ^ 0x64806480
+// in one LOP3 (bytes 1 and 3 of x are ignored).
+__device__ __forceinline__ uint32_t biased_pair_i8(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(x), "r"(0x00FF00FFu), "r"(0x64806480u));
+  return r;
+}
+
 template <int KVT>
 constexpr int elem_bytes() {
   return (KVT == FAT_DTYPE_I8 || KVT == FAT_DTYPE_E4M3) ? 1 : 2;
@@ -246,6 +270,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   constexpr int kChunk = L::kChunk;
   constexpr int kTW = L::kTW;
   constexpr int NT = D / 8;  // n-tiles of the output
+  constexpr bool kBias = std::is_same<T, __half>::value && KVT == FAT_DTYPE_I8;  // biased int8 widening
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -798,6 +823,8 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   const int ctid = tid;  // 0..127
   float o[NT][4];
   float m_run = -CUDART_INF_F, l_run = 0.f;
+  float cs_run = 0.f;  // biased int8: running sum of the p fed to P.V (rescaled like l_run)
+  float qbias = 0.f;   // biased int8: 1152 * sum(q) of row g
   uint32_t qa[D / 16][2];
   int it = 0;
   int ev = 0;  // pieces handed to the merge warp
@@ -814,6 +841,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     if (flags & kFirst) {
       m_run = -CUDART_INF_F;
       l_run = 0.f;
+      cs_run = 0.f;
 #pragma unroll
       for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
       const T* qs = reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(qarea) + size_t(s) * L::kQBytes);
@@ -824,6 +852,19 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         const int d1 = (EB == 2) ? ks * 16 + 8 + 2 * c : c * (D / 4) + 4 * ks + 2;
         qa[ks][0] = *reinterpret_cast<const uint32_t*>(qs + g * D + d0);
         qa[ks][1] = *reinterpret_cast<const uint32_t*>(qs + g * D + d1);
+      }
+      if constexpr (kBias) {
+        float sq = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          float x0, x1, x2, x3;
+          unpack2<T>(qa[ks][0], x0, x1);
+          unpack2<T>(qa[ks][1], x2, x3);
+          sq += (x0 + x1) + (x2 + x3);
+        }
+        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+        qbias = kI8Bias * sq;
       }
     }
 
@@ -890,7 +931,11 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
             for (int i = 0; i < (kSlice >= 16 ? 4 : 2); ++i) {
               const int ks = v * 4 + i;
               uint32_t b0, b1;
-              Widen<T, KVT>::run(wv[i], b0, b1);
+              if constexpr (kBias) {
+                widen_i8_biased(wv[i], b0, b1);
+              } else {
+                Widen<T, KVT>::run(wv[i], b0, b1);
+              }
               const uint32_t av[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
               MmaOp<T>::run(sacc[j], av, b0, b1);
             }
@@ -900,7 +945,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
 
       // ---- online softmax on the fragment (rows g: heads, cols: tokens) ----
       const int toks[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
-      const float sv_raw[4] = {sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]};
+      const float sv_raw[4] = {sacc[0][0] - qbias, sacc[0][1] - qbias, sacc[1][0] - qbias, sacc[1][1] - qbias};
       float sv[4];
       float ksc[2] = {1.f, 1.f}, vsc[2] = {1.f, 1.f};
       if constexpr (EB == 1) {
@@ -934,8 +979,10 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
 
       // ---- O += P V : rows 0-7 carry P rounded to 16 bits, rows 8-15 the remainder ----
       uint32_t pa[4];
-      split_hi_lo<T>(pr[0] * vsc[0], pr[1] * vsc[0], pa[0], pa[1]);
-      split_hi_lo<T>(pr[2] * vsc[1], pr[3] * vsc[1], pa[2], pa[3]);
+      const float pv[4] = {pr[0] * vsc[0], pr[1] * vsc[0], pr[2] * vsc[1], pr[3] * vsc[1]};
+      split_hi_lo<T>(pv[0], pv[1], pa[0], pa[1]);
+      split_hi_lo<T>(pv[2], pv[3], pa[2], pa[3]);
+      if constexpr (kBias) cs_run = cs_run * alpha + ((pv[0] + pv[1]) + (pv[2] + pv[3]));
       if constexpr (EB == 2) {
         const int row = wrow + ((lane >> 3) & 1) * 8 + (lane & 7);
         const int dsel = (lane >> 4) << 3;
@@ -968,6 +1015,20 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
             }
           }
         }
+        if constexpr (kBias) {
+          // Pair (row 2c, row 2c+1) and (row 2c+8, row 2c+9) of byte i: one
+          // PRMT gathers the two codes, one LOP3 makes the biased fp16 pair.
+#pragma unroll
+          for (int w = 0; w < kSlice / 4; ++w) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t sel = uint32_t(i) * 0x11u + uint32_t(4 + i) * 0x1100u;
+              const uint32_t b0 = biased_pair_i8(__byte_perm(rw[0][w], rw[1][w], sel));
+              const uint32_t b1 = biased_pair_i8(__byte_perm(rw[2][w], rw[3][w], sel));
+              MmaOp<T>::run(o[4 * w + i], pa, b0, b1);
+            }
+          }
+        } else {
 #pragma unroll
         for (int w = 0; w < kSlice / 4; ++w) {
           uint32_t b0a, b0b, b0c, b0d, b1a, b1b, b1c, b1d;
@@ -979,6 +1040,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
           MmaOp<T>::run(o[4 * w + 1], pa, b0b, b1b);
           MmaOp<T>::run(o[4 * w + 2], pa, b0c, b1c);
           MmaOp<T>::run(o[4 * w + 3], pa, b0d, b1d);
+        }
         }
       }
       if (nvalid < 16) fence_proxy_async_smem();
@@ -994,14 +1056,19 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       if (ev > 0 && !mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag)) break;
       const float l_row = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
       const float l_tot = l_row + __shfl_xor_sync(0xffffffffu, l_row, 2);
+      float corr = 0.f;  // biased int8: 1152 * sum(p) of row g over the piece
+      if constexpr (kBias) {
+        const float c_row = cs_run + __shfl_xor_sync(0xffffffffu, cs_run, 1);
+        corr = kI8Bias * (c_row + __shfl_xor_sync(0xffffffffu, c_row, 2));
+      }
       float* myO = mO + (warp * kRows + g) * (D + 8);
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         if constexpr (EB == 2) {
           *reinterpret_cast<float2*>(myO + n * 8 + 2 * c) = make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
         } else {
-          myO[(2 * c) * (D / 8) + n] = o[n][0] + o[n][2];
-          myO[(2 * c + 1) * (D / 8) + n] = o[n][1] + o[n][3];
+          myO[(2 * c) * (D / 8) + n] = (o[n][0] + o[n][2]) - corr;
+          myO[(2 * c + 1) * (D / 8) + n] = (o[n][1] + o[n][3]) - corr;
         }
       }
       if (c == 0) {
