@@ -945,7 +945,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
 
       // ---- online softmax on the fragment (rows g: heads, cols: tokens) ----
       const int toks[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
-      const float sv_raw[4] = {sacc[0][0] - qbias, sacc[0][1] - qbias, sacc[1][0] - qbias, sacc[1][1] - qbias};
+      const float sv_raw[4] = {sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]};
       float sv[4];
       float ksc[2] = {1.f, 1.f}, vsc[2] = {1.f, 1.f};
       if constexpr (EB == 1) {
@@ -955,8 +955,17 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         vsc[0] = mt.vscale[grp];
         vsc[1] = mt.vscale[grp + 1];
       }
+      // Scores in log2 units: (s - qbias) * scale * k_scale as one FMA per score.
+      const float kf[2] = {p.scale_log2 * ksc[0], p.scale_log2 * ksc[1]};
+      const float kb[2] = {-qbias * kf[0], -qbias * kf[1]};
+      if (nvalid >= 16) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sv[i] = (toks[i] < nvalid) ? sv_raw[i] * (p.scale_log2 * ksc[i >> 1]) : -CUDART_INF_F;
+        for (int i = 0; i < 4; ++i) sv[i] = fmaf(sv_raw[i], kf[i >> 1], kb[i >> 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          sv[i] = (toks[i] < nvalid) ? fmaf(sv_raw[i], kf[i >> 1], kb[i >> 1]) : -CUDART_INF_F;
+      }
       float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
