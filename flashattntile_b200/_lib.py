@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32,
          _i32, _i32, _i32, _i32, _vp, _vp],
     ),
+    "fat_cache_value_stats": (_i32, [_vp, _vp, _i64, _i32, _i64, _i32, _vp, _vp, _vp]),
     "fat_gather_paged": (
         _i32,
         [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp],
@@ -156,6 +157,7 @@ def stream_handle(device: torch.device) -> int:
 # ---------------------------------------------------------------------------
 _WS: dict[tuple[int, int], torch.Tensor] = {}
 _ERR: dict[tuple[int, int], torch.Tensor] = {}
+_STATS: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
 
 
 def workspace_for(index: int, stream: int, device: torch.device, nbytes: int) -> torch.Tensor:
@@ -195,6 +197,28 @@ def reset_workspace(device: torch.device) -> None:
         _WS[key].zero_()
     if key in _ERR:
         _ERR[key].zero_()
+
+
+def cache_value_stats(seq_lens: torch.Tensor, page_table: torch.Tensor, page_size: int) -> list[int]:
+    """``fat_cache_value_stats`` on the current stream: [min len, max len, min used
+    page id, max used page id] in one kernel and one 16-byte read-back (the
+    stream is synchronised)."""
+    lib = load()
+    dev = seq_lens.device
+    index, stream = _key(dev)
+    bufs = _STATS.get((index, stream))
+    if bufs is None:
+        bufs = (torch.zeros(4, dtype=torch.int32, device=dev), torch.zeros(4, dtype=torch.int32).pin_memory())
+        _STATS[(index, stream)] = bufs
+    if page_table.stride(1) != 1:
+        page_table = page_table.contiguous()
+    if not seq_lens.is_contiguous():
+        seq_lens = seq_lens.contiguous()
+    status = lib.fat_cache_value_stats(seq_lens.data_ptr(), page_table.data_ptr(), page_table.stride(0),
+                                       seq_lens.numel(), page_table.shape[1], int(page_size), bufs[0].data_ptr(),
+                                       bufs[1].data_ptr(), stream)
+    check(status, "cache_value_stats")
+    return bufs[1].tolist()
 
 
 def read_device_error(device: torch.device) -> int:

@@ -23,7 +23,7 @@ PKG = CSRC.parent
 ROOT = PKG.parent
 BUILD = ROOT / "_build"
 LIB = PKG / "libflashattn_sm100.so"
-SOURCES = ["decode.cu", "decode_noalloc.cu", "prefill.cu", "gather.cu", "merge.cu", "append.cu", "host_util.cpp", "capi.cpp"]
+SOURCES = ["decode.cu", "decode_noalloc.cu", "prefill.cu", "gather.cu", "merge.cu", "append.cu", "stats.cu", "host_util.cpp", "capi.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-Xptxas", "-warn-spills"]

@@ -8,6 +8,7 @@
 #include "merge.h"
 #include "append.h"
 #include "prefill.h"
+#include "stats.h"
 #include "host_util.h"
 
 extern "C" {
@@ -268,6 +269,14 @@ int fat_prefill_paged(const void* q, int64_t q_stride_t, int64_t q_stride_h, con
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
   return fat::launch_prefill_paged(a);
+}
+
+
+int fat_cache_value_stats(const int32_t* seq_lens, const int32_t* page_table, int64_t page_table_stride, int batch,
+                          int64_t max_pages, int page_size, int32_t* device_scratch, int32_t* host_out, void* stream) {
+  fat::set_last_error("");
+  return fat::cache_value_stats(seq_lens, page_table, page_table_stride, batch, max_pages, page_size, device_scratch,
+                                host_out, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from .. import _config, _lib
-from ..paging import PagedKVCache, validate_cache, validate_metadata
+from ..paging import PagedKVCache, validate_cache_values, validate_metadata
 
 DEFAULT_CONFIG = {"split_k": 1, "num_warps": 4, "num_stages": 2}
 # Import compatibility with code written against the reference: this build has
@@ -56,25 +56,44 @@ def _resolve_config(config: dict | None) -> dict:
     return resolved
 
 
-def _validate_decode_inputs(q: torch.Tensor, cache: PagedKVCache) -> None:
-    """``decode.py:503-522``: same checks, exception types and messages."""
-    if not isinstance(cache, PagedKVCache):
-        raise TypeError("cache must be a PagedKVCache")
-    stats = validate_cache(cache) if _config.validate_values() else validate_metadata(cache)
+def _q_error(q: torch.Tensor, cache: PagedKVCache) -> Exception | None:
     if q.dim() != 3:
-        raise ValueError(f"q must be [batch, heads, head_dim], got {tuple(q.shape)}")
+        return ValueError(f"q must be [batch, heads, head_dim], got {tuple(q.shape)}")
     if q.shape[0] != cache.batch_size:
-        raise ValueError(f"q batch {q.shape[0]} != cache batch {cache.batch_size}")
+        return ValueError(f"q batch {q.shape[0]} != cache batch {cache.batch_size}")
     if q.shape[2] != cache.head_dim:
-        raise ValueError(f"q head_dim {q.shape[2]} != cache head_dim {cache.head_dim}")
+        return ValueError(f"q head_dim {q.shape[2]} != cache head_dim {cache.head_dim}")
     if q.shape[1] % cache.num_kv_heads != 0:
-        raise ValueError(f"num_heads {q.shape[1]} must be divisible by num_kv_heads {cache.num_kv_heads}")
+        return ValueError(f"num_heads {q.shape[1]} must be divisible by num_kv_heads {cache.num_kv_heads}")
     if q.device != cache.k_cache.device:
-        raise ValueError("q and cache must live on the same device")
+        return ValueError("q and cache must live on the same device")
     if not q.is_floating_point():
-        raise ValueError(f"q must be floating point, got {q.dtype}")
+        return ValueError(f"q must be floating point, got {q.dtype}")
+    return None
+
+
+def _value_checks(cache: PagedKVCache) -> None:
+    """The value checks of ``decode.py:503-522`` (one device->host read-back)."""
+    if not _config.validate_values():
+        return
+    stats = validate_cache_values(cache)
     if stats is not None and stats[0] <= 0:
         raise ValueError("decode requires every sequence to hold at least one cached token")
+
+
+def _check_decode_structure(q: torch.Tensor, cache: PagedKVCache) -> None:
+    """``decode.py:503-522`` minus the value checks: every check that reads no
+    device memory, same exception types and messages.  A q error is raised after
+    the value checks, as the reference checks the cache values first; on success
+    the caller runs ``_value_checks`` last, right before the launch."""
+    if not isinstance(cache, PagedKVCache):
+        raise TypeError("cache must be a PagedKVCache")
+    validate_metadata(cache)
+    err = _q_error(q, cache)
+    if err is not None:
+        if _config.validate_values():
+            validate_cache_values(cache)
+        raise err
 
 
 def _require_cuda(*tensors: torch.Tensor) -> None:
@@ -92,16 +111,13 @@ def _aligned_q(q: torch.Tensor) -> torch.Tensor:
     return q if ok else q.contiguous()
 
 
-def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
-                  k_scale=None, v_scale=None, out=None, out_dtype=None, lse=None):
-    """Run ``fat_paged_decode`` on the current stream of q's device.
-
-    With ``lse`` (fp32 ``[B, H]``, unit stride along H) the kernel also writes
-    the base-2 log-sum-exp of each row's scaled scores (``fat_paged_decode_lse``),
-    -inf for a sequence with no cached tokens.
-
-    No host<->device synchronisation happens here; device-side problems are
-    recorded in the stream's error word (``flashattntile_b200.device_error``).
+def prepare_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
+                   k_scale=None, v_scale=None, out=None, out_dtype=None, lse=None):
+    """All of :func:`launch_decode`'s host work (checks, output, scratch, the
+    argument list) without the launch: returns a callable that launches on the
+    stream current now and returns the output.  Callers that must synchronise
+    before launching (value checks) prepare first, so the GPU waits for no host
+    work after the synchronisation.
     """
     _require_cuda(q, k_cache, v_cache, page_table, seq_lens)
     lib = _lib.load()
@@ -143,35 +159,69 @@ def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_
                 or tuple(lse.shape) != (batch, heads):
             raise ValueError(f"lse must be a float32 [{batch}, {heads}] tensor on {dev} with unit stride along heads")
         fn, args = lib.fat_paged_decode_lse, args + (lse.data_ptr(), lse.stride(0)) + tail
-    if idx == torch.cuda.current_device():
-        status = fn(*args)
-    else:
-        with torch.cuda.device(idx):
+    def fire() -> torch.Tensor:
+        if idx == torch.cuda.current_device():
             status = fn(*args)
-    _lib.check(status, "paged_decode")
-    return out
+        else:
+            with torch.cuda.device(idx):
+                status = fn(*args)
+        _lib.check(status, "paged_decode")
+        return out
+
+    return fire
+
+
+def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
+                  k_scale=None, v_scale=None, out=None, out_dtype=None, lse=None):
+    """Run ``fat_paged_decode`` on the current stream of q's device.
+
+    With ``lse`` (fp32 ``[B, H]``, unit stride along H) the kernel also writes
+    the base-2 log-sum-exp of each row's scaled scores (``fat_paged_decode_lse``),
+    -inf for a sequence with no cached tokens.
+
+    No host<->device synchronisation happens here; device-side problems are
+    recorded in the stream's error word (``flashattntile_b200.device_error``).
+    """
+    return prepare_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k,
+                          k_scale=k_scale, v_scale=v_scale, out=out, out_dtype=out_dtype, lse=lse)()
 
 
 def paged_decode_attention(q: torch.Tensor, cache: PagedKVCache, softmax_scale: float | None = None,
                            config: dict | None = None, grouped: bool = False) -> torch.Tensor:
     """One query per sequence against a paged fp16/bf16 cache -> ``[B, H, D]`` in q's dtype."""
-    _validate_decode_inputs(q, cache)
-    scale = float(softmax_scale) if softmax_scale is not None else q.shape[-1] ** -0.5
-    cfg = _resolve_config(config)
-    _require_cuda(q)
-    if q.dtype not in (torch.float16, torch.bfloat16):
-        raise NotImplementedError(f"paged decode has fp16/bf16 kernels only, got {q.dtype}")
-    if cache.k_cache.dtype != q.dtype:
-        raise ValueError(f"q dtype {q.dtype} must match cache dtype {cache.k_cache.dtype}")
+    _check_decode_structure(q, cache)
     del grouped  # every launch shares each K/V page across its GQA group
-    return launch_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size,
-                         scale, cfg["split_k"])
+    try:
+        scale = float(softmax_scale) if softmax_scale is not None else q.shape[-1] ** -0.5
+        cfg = _resolve_config(config)
+        _require_cuda(q)
+        if q.dtype not in (torch.float16, torch.bfloat16):
+            raise NotImplementedError(f"paged decode has fp16/bf16 kernels only, got {q.dtype}")
+        if cache.k_cache.dtype != q.dtype:
+            raise ValueError(f"q dtype {q.dtype} must match cache dtype {cache.k_cache.dtype}")
+        fire = prepare_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens,
+                              cache.page_size, scale, cfg["split_k"])
+    except Exception:
+        _value_checks(cache)  # the reference reports bad cache values first
+        raise
+    _value_checks(cache)
+    return fire()
 
 
 def paged_decode_attention_fp8(q: torch.Tensor, cache: PagedKVCache, scales, softmax_scale: float | None = None,
                                config: dict | None = None) -> torch.Tensor:
     """Decode against an INT8 / float8_e4m3fn cache with per-(page, KV-head) fp32 scales."""
-    _validate_decode_inputs(q, cache)
+    _check_decode_structure(q, cache)
+    try:
+        fire = _prepare_decode_fp8(q, cache, scales, softmax_scale, config)
+    except Exception:
+        _value_checks(cache)  # the reference reports bad cache values first
+        raise
+    _value_checks(cache)
+    return fire()
+
+
+def _prepare_decode_fp8(q, cache, scales, softmax_scale, config):
     k_scale = scales["k"] if isinstance(scales, dict) else scales.k
     v_scale = scales["v"] if isinstance(scales, dict) else scales.v
     if cache.k_cache.dtype not in _QUANT_DTYPES:
@@ -184,5 +234,5 @@ def paged_decode_attention_fp8(q: torch.Tensor, cache: PagedKVCache, scales, sof
     _require_cuda(q, k_scale, v_scale)
     if q.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError(f"quantised decode requires fp16/bf16 queries, got {q.dtype}")
-    return launch_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size,
-                         scale, cfg["split_k"], k_scale=k_scale.float(), v_scale=v_scale.float())
+    return prepare_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size,
+                          scale, cfg["split_k"], k_scale=k_scale.float(), v_scale=v_scale.float())

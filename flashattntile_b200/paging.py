@@ -94,6 +94,12 @@ def cache_value_stats(cache: PagedKVCache) -> tuple[int, int, int, int]:
     with no used entry the page bounds are reported as ``(0, -1)``."""
     lens = cache.seq_lens
     table = cache.page_table
+    if lens.is_cuda and table.is_cuda and lens.device == table.device:
+        # One small kernel and one 16-byte read-back instead of a dozen torch reductions.
+        from . import _lib
+
+        lo, hi, umin, umax = _lib.cache_value_stats(lens, table, cache.page_size)
+        return int(lo), int(hi), int(umin), int(umax)
     need = torch.div(lens.max().to(torch.int64) + cache.page_size - 1, cache.page_size, rounding_mode="floor")
     cols = torch.arange(table.shape[1], device=table.device)
     used = (cols < need.to(table.device))[None, :].expand_as(table)
@@ -113,6 +119,11 @@ def validate_cache(cache: PagedKVCache, *, check_pages: bool = True) -> tuple[in
     checks on ``seq_lens`` / ``page_table`` -- read back in a single device->host
     transfer.  Returns ``(min seq_len, max seq_len)`` (None for an empty batch)."""
     validate_metadata(cache)
+    return validate_cache_values(cache, check_pages=check_pages)
+
+
+def validate_cache_values(cache: PagedKVCache, *, check_pages: bool = True) -> tuple[int, int] | None:
+    """The value half of :func:`validate_cache` (metadata already checked)."""
     if cache.seq_lens.numel() == 0:
         return None
     lo, max_len, umin, umax = cache_value_stats(cache)

@@ -303,3 +303,74 @@ def test_f32_mode_precision_on_unit_scale_inputs():
     q, k, v, table, lens = paged_case(32, [4096, 1, 2, 3000], 32, 8, 128, 16)
     out32 = _run(q, k, v, table, lens, 16, out_dtype=torch.float32)
     assert_close_f32(out32, _oracle(q, k, v, table, lens, 16, torch.float16, out_f32=True), atol=ATOL_F32_MODE / 20)
+
+
+def _torch_value_stats(lens, table, ps):
+    """The torch reductions the kernel replaces (same definition of "used")."""
+    big = torch.iinfo(torch.int32).max
+    hi = int(lens.max())
+    need = max(0, -(-hi // ps)) if hi > 0 else 0
+    need = min(need, table.shape[1])
+    used = table[:, :need]
+    if used.numel() == 0:
+        return [int(lens.min()), hi, 0, -1]
+    return [int(lens.min()), hi, int(used.min()), int(used.max())]
+
+
+_STATS_CASES = ["ragged", "zeros", "negative", "clamped", "strided", "wide"]
+
+
+@pytest.mark.parametrize("case", _STATS_CASES)
+def test_cache_value_stats_kernel_matches_torch(case):
+    """fat_cache_value_stats (one kernel + 16-byte read-back) gives the statistics
+    the validation checks, exactly as the torch reductions would."""
+    from flashattntile_b200 import _lib
+
+    gen = torch.Generator().manual_seed(_STATS_CASES.index(case))
+    ps = 16
+    if case == "wide":
+        batch, max_pages = 300, 1100
+    else:
+        batch, max_pages = 37, 20
+    table = torch.randint(-3, 5000, (batch, max_pages), generator=gen, dtype=torch.int32)
+    lens = torch.randint(0, max_pages * ps, (batch,), generator=gen, dtype=torch.int32)
+    if case == "zeros":
+        lens.zero_()
+    elif case == "negative":
+        lens[5] = -7
+    elif case == "clamped":
+        lens[3] = max_pages * ps + 100  # past the capacity: the scan stops at the table's width
+    table_d = table.to(DEV)
+    if case == "strided":
+        table_d = torch.randint(0, 9, (batch, 2 * max_pages), dtype=torch.int32, device=DEV)[:, ::2]
+        table = table_d.cpu()
+    got = _lib.cache_value_stats(lens.to(DEV), table_d, ps)
+    assert got == _torch_value_stats(lens, table, ps)
+
+
+def test_validation_errors_raised_through_the_stats_kernel():
+    """The op's value checks (reference messages) still fire with the kernel path."""
+    from flashattntile_b200.paging import validate_cache
+
+    from flashattntile_b200.paging import PagedKVCache
+
+    _, k, v, table, lens = paged_case(41, [40, 70], 8, 2, 64, 16)
+    k, v, table, lens = k.to(DEV), v.to(DEV), table.to(DEV), lens.to(DEV)
+
+    cache = PagedKVCache(k, v, table.clone(), lens.clone(), 16)
+    assert validate_cache(cache) == (40, 70)
+    bad = table.clone()
+    bad[1, 0] = k.shape[0]
+    with pytest.raises(AssertionError, match="references page"):
+        validate_cache(PagedKVCache(k, v, bad, lens.clone(), 16))
+    bad[1, 0] = -1
+    with pytest.raises(AssertionError, match="negative page id"):
+        validate_cache(PagedKVCache(k, v, bad, lens.clone(), 16))
+    neg = lens.clone()
+    neg[0] = -1
+    with pytest.raises(AssertionError, match="non-negative"):
+        validate_cache(PagedKVCache(k, v, table.clone(), neg, 16))
+    over = lens.clone()
+    over[0] = table.shape[1] * 16 + 1
+    with pytest.raises(AssertionError, match="capacity"):
+        validate_cache(PagedKVCache(k, v, table.clone(), over, 16))
