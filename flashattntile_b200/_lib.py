@@ -157,7 +157,7 @@ def stream_handle(device: torch.device) -> int:
 # ---------------------------------------------------------------------------
 _WS: dict[tuple[int, int], torch.Tensor] = {}
 _ERR: dict[tuple[int, int], torch.Tensor] = {}
-_STATS: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
+_STATS: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor, torch.cuda.Event]] = {}
 
 
 def workspace_for(index: int, stream: int, device: torch.device, nbytes: int) -> torch.Tensor:
@@ -199,16 +199,19 @@ def reset_workspace(device: torch.device) -> None:
         _ERR[key].zero_()
 
 
-def cache_value_stats(seq_lens: torch.Tensor, page_table: torch.Tensor, page_size: int) -> list[int]:
-    """``fat_cache_value_stats`` on the current stream: [min len, max len, min used
-    page id, max used page id] in one kernel and one 16-byte read-back (the
-    stream is synchronised)."""
+def cache_value_stats_async(seq_lens: torch.Tensor, page_table: torch.Tensor,
+                            page_size: int) -> tuple[torch.Tensor, torch.cuda.Event]:
+    """Queue ``fat_cache_value_stats`` on the current stream: returns the pinned
+    host buffer that will hold [min len, max len, min used page id, max used page
+    id] and an event recorded after the copy (synchronise it before reading).
+    The buffer is per stream: read it before the next call on the same stream."""
     lib = load()
     dev = seq_lens.device
     index, stream = _key(dev)
     bufs = _STATS.get((index, stream))
     if bufs is None:
-        bufs = (torch.zeros(4, dtype=torch.int32, device=dev), torch.zeros(4, dtype=torch.int32).pin_memory())
+        bufs = (torch.zeros(4, dtype=torch.int32, device=dev), torch.zeros(4, dtype=torch.int32).pin_memory(),
+                torch.cuda.Event())
         _STATS[(index, stream)] = bufs
     if page_table.stride(1) != 1:
         page_table = page_table.contiguous()
@@ -218,7 +221,15 @@ def cache_value_stats(seq_lens: torch.Tensor, page_table: torch.Tensor, page_siz
                                        seq_lens.numel(), page_table.shape[1], int(page_size), bufs[0].data_ptr(),
                                        bufs[1].data_ptr(), stream)
     check(status, "cache_value_stats")
-    return bufs[1].tolist()
+    bufs[2].record(torch.cuda.current_stream(dev))
+    return bufs[1], bufs[2]
+
+
+def cache_value_stats(seq_lens: torch.Tensor, page_table: torch.Tensor, page_size: int) -> list[int]:
+    """:func:`cache_value_stats_async`, waited for."""
+    host, event = cache_value_stats_async(seq_lens, page_table, page_size)
+    event.synchronize()
+    return host.tolist()
 
 
 def read_device_error(device: torch.device) -> int:

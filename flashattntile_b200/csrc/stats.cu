@@ -88,8 +88,6 @@ int cache_value_stats(const int32_t* seq_lens, const int32_t* page_table, int64_
   if (e != cudaSuccess) return cuda_failure("cache_stats_kernel launch", e);
   e = cudaMemcpyAsync(host_out, device_scratch, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
   if (e != cudaSuccess) return cuda_failure("cudaMemcpyAsync(cache stats)", e);
-  e = cudaStreamSynchronize(stream);
-  if (e != cudaSuccess) return cuda_failure("cudaStreamSynchronize(cache stats)", e);
   return FAT_OK;
 }
 

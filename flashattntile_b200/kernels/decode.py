@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from .. import _config, _lib
-from ..paging import PagedKVCache, validate_cache_values, validate_metadata
+from ..paging import PagedKVCache, check_value_stats, validate_cache_values, validate_metadata
 
 DEFAULT_CONFIG = {"split_k": 1, "num_warps": 4, "num_stages": 2}
 # Import compatibility with code written against the reference: this build has
@@ -76,16 +76,40 @@ def _value_checks(cache: PagedKVCache) -> None:
     """The value checks of ``decode.py:503-522`` (one device->host read-back)."""
     if not _config.validate_values():
         return
-    stats = validate_cache_values(cache)
+    _check_lengths(validate_cache_values(cache))
+
+
+def _check_lengths(stats) -> None:
     if stats is not None and stats[0] <= 0:
         raise ValueError("decode requires every sequence to hold at least one cached token")
+
+
+def _run_checked(cache: PagedKVCache, fire):
+    """Launch ``fire`` and apply the value checks, raising the reference's error
+    (type and message) before returning.  On CUDA the statistics are queued
+    first and the kernel right behind them, so the GPU does not idle while the
+    host waits for the 16-byte read-back; the kernel is memory-safe on any
+    metadata (page ids outside the pool are skipped and reported on the device,
+    lengths are bounded by the page table), so an invalid call only costs an
+    unused output before it raises."""
+    lens, table = cache.seq_lens, cache.page_table
+    if not _config.validate_values() or lens.numel() == 0:
+        return fire()
+    if not (lens.is_cuda and table.is_cuda and lens.device == table.device):
+        _value_checks(cache)
+        return fire()
+    host, event = _lib.cache_value_stats_async(lens, table, cache.page_size)
+    out = fire()
+    event.synchronize()
+    _check_lengths(check_value_stats(cache, host.tolist()))
+    return out
 
 
 def _check_decode_structure(q: torch.Tensor, cache: PagedKVCache) -> None:
     """``decode.py:503-522`` minus the value checks: every check that reads no
     device memory, same exception types and messages.  A q error is raised after
     the value checks, as the reference checks the cache values first; on success
-    the caller runs ``_value_checks`` last, right before the launch."""
+    the caller applies the value checks around the launch (``_run_checked``)."""
     if not isinstance(cache, PagedKVCache):
         raise TypeError("cache must be a PagedKVCache")
     validate_metadata(cache)
@@ -204,8 +228,7 @@ def paged_decode_attention(q: torch.Tensor, cache: PagedKVCache, softmax_scale: 
     except Exception:
         _value_checks(cache)  # the reference reports bad cache values first
         raise
-    _value_checks(cache)
-    return fire()
+    return _run_checked(cache, fire)
 
 
 def paged_decode_attention_fp8(q: torch.Tensor, cache: PagedKVCache, scales, softmax_scale: float | None = None,
@@ -217,8 +240,7 @@ def paged_decode_attention_fp8(q: torch.Tensor, cache: PagedKVCache, scales, sof
     except Exception:
         _value_checks(cache)  # the reference reports bad cache values first
         raise
-    _value_checks(cache)
-    return fire()
+    return _run_checked(cache, fire)
 
 
 def _prepare_decode_fp8(q, cache, scales, softmax_scale, config):

@@ -126,7 +126,12 @@ def validate_cache_values(cache: PagedKVCache, *, check_pages: bool = True) -> t
     """The value half of :func:`validate_cache` (metadata already checked)."""
     if cache.seq_lens.numel() == 0:
         return None
-    lo, max_len, umin, umax = cache_value_stats(cache)
+    return check_value_stats(cache, cache_value_stats(cache), check_pages=check_pages)
+
+
+def check_value_stats(cache: PagedKVCache, stats, *, check_pages: bool = True) -> tuple[int, int]:
+    """The assertions of the value checks on ``cache_value_stats`` numbers."""
+    lo, max_len, umin, umax = (int(x) for x in stats)
     _assert(lo >= 0, "seq_lens must be non-negative")
     _assert(max_len <= cache.capacity, f"seq_len {max_len} exceeds page-table capacity {cache.capacity}")
     if check_pages and max_len > 0:

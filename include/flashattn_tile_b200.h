@@ -240,10 +240,11 @@ int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_pa
  * flashattn_tile/paging.py:84-130 (validate_cache): host_out[0..3] = min and max
  * of seq_lens[batch], then min and max of the page-table entries a sequence of
  * the maximum length reaches (the first ceil(max / page_size) columns of every
- * row, at most max_pages; (0, -1) when there are none).  One kernel on `stream`,
+ * row, at most max_pages; (0, -1) when there are none).  Queues one kernel and
  * a 16-byte copy into host_out (host memory, pinned for an asynchronous copy)
- * and a synchronisation of `stream`.  device_scratch: 4 int32 on the device.
- * Replaces the reference's torch reductions + read-back of both tensors.
+ * on `stream`; synchronise the stream (or an event recorded after this call)
+ * before reading host_out.  device_scratch: 4 int32 on the device.  Replaces
+ * the reference's torch reductions + read-back of both tensors.
  */
 int fat_cache_value_stats(const int32_t* seq_lens, const int32_t* page_table, int64_t page_table_stride, int batch,
                           int64_t max_pages, int page_size, int32_t* device_scratch, int32_t* host_out, void* stream);

@@ -374,3 +374,55 @@ def test_validation_errors_raised_through_the_stats_kernel():
     over[0] = table.shape[1] * 16 + 1
     with pytest.raises(AssertionError, match="capacity"):
         validate_cache(PagedKVCache(k, v, table.clone(), over, 16))
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_op_raises_reference_errors_with_overlapped_checks(quant):
+    """The op queues the value statistics, launches, then raises the reference's
+    error before returning; the kernel itself never faults on the bad metadata."""
+    import flashattntile_b200
+    from flashattntile_b200.kernels.decode import paged_decode_attention, paged_decode_attention_fp8
+    from flashattntile_b200.paging import PagedKVCache
+
+    q, k, v, table, lens = paged_case(43, [40, 70, 9], 8, 2, 64, 16)
+    q, k, v, table, lens = q.to(DEV), k.to(DEV), v.to(DEV), table.to(DEV), lens.to(DEV)
+    scales = None
+    if quant:
+        k, v = k.to(torch.int8), v.to(torch.int8)
+        ones = torch.ones(k.shape[0], k.shape[2], device=DEV)
+        scales = {"k": ones, "v": ones}
+
+    def run(table_, lens_, q_=q):
+        cache = PagedKVCache(k, v, table_, lens_, 16)
+        if quant:
+            return paged_decode_attention_fp8(q_, cache, scales)
+        return paged_decode_attention(q_, cache)
+
+    good = run(table, lens)
+    torch.cuda.synchronize()
+    bad = table.clone()
+    bad[1, 2] = k.shape[0] + 5
+    with pytest.raises(AssertionError, match="references page"):
+        run(bad, lens)
+    bad[1, 2] = -4
+    with pytest.raises(AssertionError, match="negative page id"):
+        run(bad, lens)
+    over = lens.clone()
+    over[0] = table.shape[1] * 16 + 3
+    with pytest.raises(AssertionError, match="capacity"):
+        run(table, over)
+    zero = lens.clone()
+    zero[2] = 0
+    with pytest.raises(ValueError, match="at least one cached token"):
+        run(table, zero)
+    # A q error as well: the cache values are reported first, as in the reference.
+    with pytest.raises(AssertionError, match="negative page id"):
+        run(bad, lens, q[:, :, :32])
+    with pytest.raises(ValueError, match="head_dim"):
+        run(table, lens, q[:, :, :32])
+    torch.cuda.synchronize()
+    flashattntile_b200.device_error()  # the invalid launches recorded bad pages: clear the word
+    again = run(table, lens)
+    torch.cuda.synchronize()
+    assert torch.equal(again, good)
+    assert flashattntile_b200.device_error() == 0
