@@ -46,7 +46,7 @@ constexpr int kProducers = 2;              // producer warps (take turns by chun
 constexpr int kMaxChunk = 256;             // largest chunk (tokens per pipeline stage) of any layout
 constexpr int kMaxBoxes = 32;              // TMA row boxes per chunk at most (chunk / 8)
 constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
-constexpr int kStageBudget = 160 * 1024;   // shared memory for the stage ring
+constexpr size_t kSmemMax = 227 * 1024;    // shared memory per CTA (opt-in maximum)
 
 enum : int { kFirst = 1, kLast = 2, kFull = 4, kDone = 8 };
 
@@ -61,9 +61,12 @@ struct RingInfo {
   int b, unit_local, chunk, len, chunks_b, nbox;
   long long S;
 };
-constexpr int kRingBytes = kRing * int(sizeof(RingInfo)) + kRing * kMaxBoxes * 4 * 3;
+// Per-producer prefetch ring: unit info, page ids and (8-bit caches) the pages' K/V scales.
+constexpr int ring_bytes(int eb) { return kRing * int(sizeof(RingInfo)) + kRing * kMaxBoxes * 4 * (eb == 1 ? 3 : 1); }
 
-struct Meta {
+// Per-stage metadata; the per-8-token scales exist for 8-bit caches only.
+template <int EB>
+struct alignas(16) MetaT {
   int flags;
   int b;
   int unit_local;  // kv_head * head_groups + head_group
@@ -71,8 +74,8 @@ struct Meta {
   int seq_len;
   int chunks_b;    // chunks per unit of this sequence
   long long unit_base;  // flattened index of the unit's first chunk
-  float kscale[kMaxChunk / 8];
-  float vscale[kMaxChunk / 8];
+  float kscale[EB == 1 ? kMaxChunk / 8 : 1];
+  float vscale[EB == 1 ? kMaxChunk / 8 : 1];
 };
 
 // A finished piece, handed from the consumer warps to the merge warp.
@@ -124,13 +127,20 @@ struct Layout {
   static_assert(kChunk <= kMaxChunk, "chunk larger than the per-stage metadata");
   static constexpr int kTile = kChunk * kRowBytes;                 // K (or V) bytes per stage
   static constexpr int kStage = 2 * kTile;
-  static constexpr int kStages = (kStageBudget / kStage) > 8 ? 8 : (kStageBudget / kStage);
   static constexpr int kQBytes = kRows * D * 2;
   static constexpr int kMergeFloats = kWarps * kRows * (D + 8) + 2 * kWarps * kRows;
-  static constexpr size_t kSmem = 1024 /*align slack*/ + size_t(kStages) * kStage + size_t(kStages) * kQBytes +
-                                  size_t(kStages) * sizeof(Meta) + size_t(kMergeFloats) * 4 +
-                                  size_t(2 * kStages + 2) * 8 + 64 + sizeof(MergeEvent) + size_t(kThreads) * 16 +
-                                  size_t(kProducers) * kRingBytes + 16;
+  static constexpr int kRingBytes = ring_bytes(EB);
+  using Meta = MetaT<EB>;
+  // As many stages (up to 8) as shared memory holds: bytes in flight per SM
+  // set the streaming rate (5 -> 4 stages of 32 KB cost 3.5% at cfg2).  The
+  // prologue's scan buffer lives in the (then idle) first stage.
+  static constexpr size_t kFixed = 1024 /*align slack*/ + size_t(kMergeFloats) * 4 + 2 * 8 /*merge barriers*/ +
+                                   64 + sizeof(MergeEvent) + size_t(kProducers) * kRingBytes + 16;
+  static constexpr size_t kPerStage = size_t(kStage) + kQBytes + sizeof(Meta) + 2 * 8 /*full, empty*/;
+  static constexpr int kStages = (kSmemMax - kFixed) / kPerStage > 8 ? 8 : int((kSmemMax - kFixed) / kPerStage);
+  static_assert(kStages >= 2, "decode stage ring needs two stages");
+  static_assert(size_t(kThreads + kThreads / 32) * 8 <= size_t(kStage), "prologue scan must fit in one stage");
+  static constexpr size_t kSmem = kFixed + size_t(kStages) * kPerStage;
 
   // Shared address of byte column `bc` (16-byte aligned part) of token row `row`
   // of a tile stored as [row][kCB column blocks][128 B]: with the 128-byte
@@ -276,6 +286,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
   T* qarea = reinterpret_cast<T*>(smem + size_t(kStages) * L::kStage);
+  using Meta = typename L::Meta;
   Meta* meta = reinterpret_cast<Meta*>(reinterpret_cast<uint8_t*>(qarea) + size_t(kStages) * L::kQBytes);
   float* mO = reinterpret_cast<float*>(meta + kStages);
   float* mM = mO + kWarps * kRows * (D + 8);
@@ -284,9 +295,9 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 2);  // [0] abort
   long long* shl = reinterpret_cast<long long*>(const_cast<int*>(shi) + 4);   // [0] start_b [1] start_S [2] total
   volatile MergeEvent* evt = reinterpret_cast<volatile MergeEvent*>(shl + 4);
-  long long* scan = reinterpret_cast<long long*>(const_cast<MergeEvent*>(evt) + 1);  // [kThreads]
+  long long* scan = reinterpret_cast<long long*>(stages);  // [kThreads + kThreads / 32], prologue only
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(scan + kThreads + kThreads / 32) + 15) & ~uintptr_t(15));  // producer prefetch ring
+      (reinterpret_cast<uintptr_t>(const_cast<MergeEvent*>(evt) + 1) + 15) & ~uintptr_t(15));  // producer prefetch ring
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -395,7 +406,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     const int n = int(x1 - x0);  // chunks of this CTA (fits in 32 bits)
     const int n_own = n > pid ? (n - pid + kProducers - 1) / kProducers : 0;
     int own_issued = 0;
-    RingInfo* rinfo = reinterpret_cast<RingInfo*>(ring_base + pid * kRingBytes);
+    RingInfo* rinfo = reinterpret_cast<RingInfo*>(ring_base + pid * L::kRingBytes);
     int* rids = reinterpret_cast<int*>(rinfo + kRing);
     float* rks = reinterpret_cast<float*>(rids + kRing * kMaxBoxes);
     float* rvs = rks + kRing * kMaxBoxes;
