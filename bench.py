@@ -198,8 +198,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--only", choices=["decode", "quant", "prefill", "longctx", "loop"], default=None,
-                    help="run one workload (profiling); decode = the headline line without secondary")
+    ap.add_argument("--only", choices=["decode", "quant", "prefill", "longctx", "loop", "comparators"], default=None,
+                    help="run one workload (profiling); decode = the headline line without secondary; "
+                         "comparators = library kernels on cfg2/cfg3 beside ours (never in the default run)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -226,7 +227,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     peaks = _peaks()
-    if args.only in ("quant", "prefill", "longctx", "loop"):
+    if args.only in ("quant", "prefill", "longctx", "loop", "comparators"):
         res = run_secondary(device, args, peaks, which=(args.only,), dist=dist)
         if rank == 0:
             print(json.dumps({"only": args.only, "steps": args.steps, "warmup": args.warmup, "results": res}),
@@ -351,6 +352,105 @@ def run_secondary(device, args, peaks, which=("quant", "prefill", "longctx", "lo
         res.update(run_prefill(device, args, peaks))
     if "longctx" in which:
         res.update(run_longctx(device, args, peaks, dist))
+    if "comparators" in which:
+        res.update(run_comparators(device, args, peaks))
+    return res
+
+
+def run_comparators(device, args, peaks) -> dict:
+    """Same-box library kernels beside ours, reported, not targets: flashinfer's
+    trtllm-gen and fa2 (tensor-core) paged decode on cfg2, torch SDPA (one call per
+    sequence, GQA) and flash_attn 2 varlen on cfg3.  Timed like our kernels
+    (CUDA events, cfg3 alternating two input sets); each also reports its largest
+    difference from our output.  A library that fails to run is reported with
+    its error.  First calls may JIT-compile, outside the timed region."""
+    from flashattntile_b200.autotune import flops_attention_varlen
+    from flashattntile_b200.kernels.decode import launch_decode
+    from flashattntile_b200.kernels.prefill import launch_prefill
+
+    res = {}
+    steps = max(20, args.steps // 2)
+    c = CFG2
+    q, k, v, table, lens = make_decode_cfg2(device, seed=1)
+    nbytes = decode_bytes([c["ctx"]] * c["batch"], c["heads"], c["kv_heads"], c["head_dim"], c["page_size"])
+    scale = c["head_dim"] ** -0.5
+    ours = launch_decode(q, k, v, table, lens, c["page_size"], scale, 1)
+    out = torch.empty_like(q)
+
+    def record(name, fn, ref, work, unit):
+        try:
+            o = fn()
+            torch.cuda.synchronize()
+            diff = float((o.float() - ref.float()).abs().max())
+            ms = statistics.mean(time_steps(fn, steps, args.warmup, None))
+            val = work / (ms * 1e-3) / (1e9 if unit == "GB/s" else 1e12)
+            res[name] = {"value": round(val, 1), "unit": unit, "ms": round(ms, 4), "maxdiff_vs_ours": diff}
+        except Exception as e:  # a library missing or failing on this box
+            res[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+
+    record("cfg2_decode_ours", lambda: launch_decode(q, k, v, table, lens, c["page_size"], scale, 1, out=out),
+           ours, nbytes, "GB/s")
+    try:
+        import flashinfer
+
+        ws = torch.zeros(256 << 20, dtype=torch.uint8, device=device)
+        record("cfg2_decode_flashinfer_trtllm_gen",
+               lambda: flashinfer.decode.trtllm_batch_decode_with_kv_cache(
+                   q, (k, v), ws, table, lens, c["ctx"], bmm1_scale=scale, bmm2_scale=1.0, kv_layout="NHD"),
+               ours, nbytes, "GB/s")
+        B, P = table.shape
+        w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD", use_tensor_cores=True)
+        w.plan(torch.arange(B + 1, device=device, dtype=torch.int32) * P, table.reshape(-1).contiguous(),
+               torch.full((B,), c["page_size"], dtype=torch.int32, device=device), c["heads"], c["kv_heads"],
+               c["head_dim"], c["page_size"], q_data_type=q.dtype, kv_data_type=k.dtype, sm_scale=scale)
+        record("cfg2_decode_flashinfer_fa2_tc", lambda: w.run(q, (k, v)), ours, nbytes, "GB/s")
+    except Exception as e:
+        res["cfg2_decode_flashinfer"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    del q, k, v, table, lens, ours, out
+
+    lens3 = [512, 1024, 2048, 4096]
+    flops = flops_attention_varlen(32, 128, lens3, lens3, causal=True)
+    offs = [0] + torch.tensor(lens3).cumsum(0).tolist()
+    cu = torch.tensor(offs, dtype=torch.int32, device=device)
+    g3 = torch.Generator(device=device).manual_seed(2)
+    sets = []
+    for _ in range(2):
+        sets.append(tuple(torch.randn((offs[-1], h, 128), generator=g3, device=device).half() for h in (32, 8, 8)))
+    ref3 = launch_prefill(*sets[1], cu, cu, 4096, 4096, True, 128 ** -0.5)
+    def alternate(call):
+        state = {"i": 0}  # the first call uses sets[1], the set ref3 was computed on
+
+        def fn():
+            state["i"] += 1
+            return call(*sets[state["i"] & 1])
+        return fn
+
+    o3 = torch.empty_like(sets[0][0])
+    record("cfg3_prefill_ours", alternate(lambda q3, k3, v3: launch_prefill(q3, k3, v3, cu, cu, 4096, 4096, True,
+                                                                            128 ** -0.5, out=o3)),
+           ref3, flops, "TFLOP/s")
+
+    def sdpa(q3, k3, v3):
+        import torch.nn.functional as F
+
+        outs = []
+        for a, b in zip(offs[:-1], offs[1:]):
+            o = F.scaled_dot_product_attention(q3[a:b].transpose(0, 1)[None], k3[a:b].transpose(0, 1)[None],
+                                               v3[a:b].transpose(0, 1)[None], is_causal=True, scale=128 ** -0.5,
+                                               enable_gqa=True)
+            outs.append(o[0].transpose(0, 1))
+        return torch.cat(outs)
+
+    record("cfg3_prefill_torch_sdpa", alternate(sdpa), ref3, flops, "TFLOP/s")
+    try:
+        from flash_attn import flash_attn_varlen_func
+
+        record("cfg3_prefill_flash_attn2",
+               alternate(lambda q3, k3, v3: flash_attn_varlen_func(q3, k3, v3, cu, cu, 4096, 4096,
+                                                                   softmax_scale=128 ** -0.5, causal=True)),
+               ref3, flops, "TFLOP/s")
+    except Exception as e:
+        res["cfg3_prefill_flash_attn2"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
     return res
 
 
