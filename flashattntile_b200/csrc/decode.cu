@@ -394,6 +394,9 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     // pid, pid + kProducers, ... of this CTA's range, so the per-chunk
     // bookkeeping of one warp overlaps with the others' TMA traffic.
     const int pid = warp - kWarps;
+    // K/V bytes are read once: evict-first keeps the 0.5-4 GB stream from
+    // churning L2 (+3% at cfg2 over the default policy).
+    const uint64_t kv_policy = policy_evict_first();
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
           if (j < 2 * nbox && ph >= 0) {
             const int t = tok0 + box * p.box_rows;
             const uint32_t dst = st + uint32_t(tensor) * L::kTile + uint32_t(box * p.box_rows * L::kRowBytes);
-            tma_load_5d(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph);
+            tma_load_5d_hint(dst, tensor ? &tm_v : &tm_k, fb, 0, 0, kvh, t % p.page_size, ph, kv_policy);
           }
         }
         if (first) {
