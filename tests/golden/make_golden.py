@@ -156,7 +156,7 @@ def make_cases(ref_root: Path) -> dict[str, dict[str, np.ndarray]]:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference", help="FlashAttnTile checkout to run")
+    ap.add_argument("--reference", required=True, help="path of the FlashAttnTile checkout to run")
     args = ap.parse_args()
     cases = make_cases(Path(args.reference))
     for name, arrays in cases.items():
