@@ -70,21 +70,37 @@ def _assert(condition: bool, message: str) -> None:
 
 
 def validate_metadata(cache: PagedKVCache) -> None:
-    """Shape / dtype / device checks only: never reads device memory."""
-    _assert(isinstance(cache, PagedKVCache), "cache must be a PagedKVCache")
+    """Shape / dtype / device checks only: never reads device memory.  Messages
+    are built only when a check fails (this runs on every call)."""
+    if not isinstance(cache, PagedKVCache):
+        raise AssertionError("cache must be a PagedKVCache")
     k, v = cache.k_cache, cache.v_cache
-    _assert(k.dim() == 4, f"k_cache must be 4-D [pages, page_size, kv_heads, dim], got {tuple(k.shape)}")
-    _assert(k.shape == v.shape, f"k_cache {tuple(k.shape)} and v_cache {tuple(v.shape)} must match")
-    _assert(k.dtype == v.dtype, f"k_cache dtype {k.dtype} != v_cache dtype {v.dtype}")
-    _assert(k.device == v.device, "k_cache and v_cache must live on the same device")
-    _assert(cache.page_size > 0, "page_size must be positive")
-    _assert(k.shape[1] == cache.page_size, f"k_cache page dim {k.shape[1]} != page_size {cache.page_size}")
-    _assert(cache.page_table.dtype == torch.int32, f"page_table must be int32, got {cache.page_table.dtype}")
-    _assert(cache.seq_lens.dtype == torch.int32, f"seq_lens must be int32, got {cache.seq_lens.dtype}")
-    _assert(cache.page_table.dim() == 2, "page_table must be [batch, max_pages_per_seq]")
-    _assert(cache.seq_lens.dim() == 1, "seq_lens must be [batch]")
-    _assert(cache.page_table.shape[0] == cache.seq_lens.shape[0], "page_table and seq_lens batch dimensions disagree")
-    _assert(cache.page_table.device == cache.seq_lens.device, "page_table and seq_lens must live on the same device")
+    kshape = k.shape
+    if len(kshape) != 4:
+        raise AssertionError(f"k_cache must be 4-D [pages, page_size, kv_heads, dim], got {tuple(kshape)}")
+    if kshape != v.shape:
+        raise AssertionError(f"k_cache {tuple(kshape)} and v_cache {tuple(v.shape)} must match")
+    if k.dtype != v.dtype:
+        raise AssertionError(f"k_cache dtype {k.dtype} != v_cache dtype {v.dtype}")
+    if k.device != v.device:
+        raise AssertionError("k_cache and v_cache must live on the same device")
+    if cache.page_size <= 0:
+        raise AssertionError("page_size must be positive")
+    if kshape[1] != cache.page_size:
+        raise AssertionError(f"k_cache page dim {kshape[1]} != page_size {cache.page_size}")
+    table, lens = cache.page_table, cache.seq_lens
+    if table.dtype != torch.int32:
+        raise AssertionError(f"page_table must be int32, got {table.dtype}")
+    if lens.dtype != torch.int32:
+        raise AssertionError(f"seq_lens must be int32, got {lens.dtype}")
+    if table.dim() != 2:
+        raise AssertionError("page_table must be [batch, max_pages_per_seq]")
+    if lens.dim() != 1:
+        raise AssertionError("seq_lens must be [batch]")
+    if table.shape[0] != lens.shape[0]:
+        raise AssertionError("page_table and seq_lens batch dimensions disagree")
+    if table.device != lens.device:
+        raise AssertionError("page_table and seq_lens must live on the same device")
 
 
 def cache_value_stats(cache: PagedKVCache) -> tuple[int, int, int, int]:
