@@ -1033,8 +1033,10 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
               asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
                            : "=r"(rw[r][v]), "=r"(rw[r][v + 1]), "=r"(rw[r][v + 2]), "=r"(rw[r][v + 3])
                            : "r"(a));
-            } else {
+            } else if constexpr (kSlice >= 8) {
               asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(rw[r][v]), "=r"(rw[r][v + 1]) : "r"(a));
+            } else {
+              asm volatile("ld.shared.u32 %0, [%1];" : "=r"(rw[r][v]) : "r"(a));
             }
           }
         }
@@ -1215,6 +1217,8 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
 template <typename T, int KVT>
 int dispatch_dim(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   switch (a.head_dim) {
+    case 32:
+      return launch_t<T, 32, KVT>(a, device, grid, ws);
     case 64:
       return launch_t<T, 64, KVT>(a, device, grid, ws);
     case 128:
@@ -1222,7 +1226,7 @@ int dispatch_dim(const DecodeArgs& a, int device, int grid, const WsLayout& ws) 
     case 256:
       return launch_t<T, 256, KVT>(a, device, grid, ws);
     default:
-      return unsupported("paged_decode: head_dim must be 64, 128 or 256, got " + std::to_string(a.head_dim));
+      return unsupported("paged_decode: head_dim must be 32, 64, 128 or 256, got " + std::to_string(a.head_dim));
   }
 }
 

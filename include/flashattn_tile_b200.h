@@ -88,7 +88,7 @@ size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int
  *   seq_lens   int32 [batch]; a sequence of length 0 produces zeros
  *   out        [batch, num_heads, head_dim]          out_dtype (= q_dtype, or F32)
  *
- * head_dim in {64, 128, 256}; page_size 8 or a multiple of 16 up to 256; K/V
+ * head_dim in {32, 64, 128, 256}; page_size 8 or a multiple of 16 up to 256; K/V
  * base addresses 16-byte aligned and their page/slot/head strides multiples of
  * 16 bytes.  split_k_hint (1..64) is accepted for interface compatibility: the
  * kernel chooses its own balanced split of the pages over all SMs, and the

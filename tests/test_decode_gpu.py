@@ -98,7 +98,7 @@ def test_decode_matrix_fp16(page_size, batch, split_k):
     assert_parity_16bit(out, _oracle(q, k, v, table, lens, page_size, torch.float16), torch.float16)
 
 
-@pytest.mark.parametrize("head_dim", [64, 128, 256])
+@pytest.mark.parametrize("head_dim", [32, 64, 128, 256])
 @pytest.mark.parametrize("heads,kv_heads", [(8, 8), (8, 2), (8, 1), (32, 1), (64, 8), (12, 4)])
 @pytest.mark.parametrize("page_size", [8, 16, 64])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -200,7 +200,7 @@ def test_bad_page_id_is_reported_on_device_not_faulted():
 # --------------------------------------------------------------------------- quantised
 @pytest.mark.parametrize("mode", ["int8", "float8_e4m3fn"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("head_dim,page_size", [(64, 16), (128, 32), (128, 16), (256, 64)])
+@pytest.mark.parametrize("head_dim,page_size", [(32, 8), (64, 16), (128, 32), (128, 16), (256, 64)])
 def test_quantised_decode_matches_dequantised_oracle(mode, dtype, head_dim, page_size):
     lens = [1, 17, 255, 1000]
     q, k, v, table, lens = paged_case(13, lens, 8, 2, head_dim, page_size, torch.float32)
