@@ -24,9 +24,14 @@
 // V_{j-1} by the same thread, and tcgen05.mma operations of one thread execute
 // in issue order, so the completion of S_t(j) also means O_t holds every
 // earlier P.V (the softmax may rescale O_t as soon as it sees S_t(j)).
+// head_dim 256 uses one query tile per CTA (warps 0-3 softmax, 4 producer,
+// 5 MMA issuer; S in columns [0,128), O in [128,384); single K and V buffers of
+// 64 KB), the same code with the second tile absent.
 // Every wait is bounded; on a timeout the CTA records FAT_DEVERR_TIMEOUT,
 // drains its copies and MMAs, frees tensor memory and exits.
 #include <math_constants.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -38,19 +43,8 @@ namespace pre {
 
 constexpr int BM = 128;    // query rows per tile (the MMA's M)
 constexpr int BN = 128;    // keys per K/V tile
-constexpr int kTiles = 2;  // query tiles per CTA
-constexpr int kRowsPerCta = BM * kTiles;
 constexpr int kSoftmaxThreads = 128;  // per tile
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 12 * 32;
 constexpr uint32_t kTmemCols = 512;
-// Register split: launched at 168 per thread (65536 / 384, rounded to 8); the
-// third warpgroup (producer, MMA, 2 idle warps) drops to 88 and the two
-// softmax warpgroups rise to 208: 2*128*208 + 128*88 = 64512 = 384 * 168.
-constexpr int kRegsSoftmax = 208;
-constexpr int kRegsOther = 88;
-static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * 168, "register split exceeds the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 without rescaling
 
 struct Params {
@@ -71,16 +65,35 @@ struct Params {
   const int* seq_lens_k;
 };
 
+// head_dim <= 128: two 128-row query tiles per CTA in ping-pong (S0, S1, O0,
+// O1 fill the 512 tensor-memory columns).  head_dim 256: one tile per CTA (S in
+// 128 columns, O in 256) with single K and V buffers (64 KB tiles).
 template <int D>
 struct Layout {
+  static constexpr int kTiles = D <= 128 ? 2 : 1;  // query tiles per CTA
+  static constexpr int kRowsPerCta = BM * kTiles;
+  static constexpr int kProducerWarp = 4 * kTiles;
+  static constexpr int kMmaWarp = kProducerWarp + 1;
+  static constexpr int kThreads = (4 * kTiles + 4) * 32;  // softmax warpgroup(s) + {producer, MMA, 2 idle}
+  // Two tiles: launched at 168 registers (65536 / 384, rounded to 8); the last
+  // warpgroup (producer, MMA, 2 idle warps) drops to 88 and the two softmax
+  // warpgroups rise to 208: 2*128*208 + 128*88 = 64512 = 384 * 168.  One tile
+  // (256 threads) needs no split.
+  static constexpr bool kSplitRegs = kTiles == 2;
+  static constexpr int kRegsSoftmax = 208;
+  static constexpr int kRegsOther = 88;
+  static_assert(!kSplitRegs || 2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * 168,
+                "register split exceeds the launch");
   static constexpr int kCB = D / 64;        // 128-byte column blocks (16-bit elements)
   static constexpr int kTile = BM * D * 2;  // one Q, K or V tile
-  static constexpr int kStagesK = D <= 64 ? 4 : 3;
-  static constexpr int kStagesV = D <= 64 ? 4 : 2;
+  static constexpr int kStagesK = D <= 64 ? 4 : (D <= 128 ? 3 : 1);
+  static constexpr int kStagesV = D <= 64 ? 4 : (D <= 128 ? 2 : 1);
   static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 2 * kTiles + 2) + 16;
   static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
-  static constexpr uint32_t kColS = 0;    // S_t at column kColS + 128 t
-  static constexpr uint32_t kColO = 256;  // O_t at columns [256 + 128 t, 256 + 128 t + D)
+  static_assert(kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
+  static constexpr uint32_t kColS = 0;               // S_t at column kColS + 128 t
+  static constexpr uint32_t kColO = 128 * kTiles;    // O_t at columns [kColO + 128 t, kColO + 128 t + D)
+  static_assert(kColO + 128 * (kTiles - 1) + D <= kTmemCols, "tensor memory overflow");
 };
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -110,11 +123,13 @@ __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int c
 // kPaged: K/V come from a paged cache through the page table (4-D maps
 // {head_dim, kv head, slot, page}); otherwise from packed [tokens, heads, dim].
 template <typename T, int D, bool kPaged>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
   using L = Layout<D>;
   constexpr int SK = L::kStagesK, SV = L::kStagesV;
+  constexpr int kTiles = L::kTiles, kRowsPerCta = L::kRowsPerCta;
+  constexpr int kProducerWarp = L::kProducerWarp, kMmaWarp = L::kMmaWarp;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdescQK = tc::idesc_f16(BM, BN, fmt, 0, 0);
   constexpr uint32_t kIdescPV = tc::idesc_f16(BM, D, fmt, 0, 1);
@@ -130,9 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kvh = h / p.group;
   const int offset = kv_len - q_len;  // bottom-right causal alignment
   const int n0 = tiles_needed(m0, q_len, kv_len, p.causal);
-  const int n1 = tiles_needed(m0 + BM, q_len, kv_len, p.causal);
+  const int n1 = kTiles > 1 ? tiles_needed(m0 + BM, q_len, kv_len, p.causal) : 0;
   const int n_max = max(n0, n1);
-  const int q_tiles = (m0 + BM < q_len) ? 2 : 1;
+  const int q_tiles = (kTiles > 1 && m0 + BM < q_len) ? 2 : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -184,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp >= kProducerWarp) {
-    regs_dec<kRegsOther>();
+    if constexpr (L::kSplitRegs) regs_dec<L::kRegsOther>();
     if (!kPaged && warp == kProducerWarp && lane == 0 && n_max > 0) {
       // ======================= TMA producer (packed K/V) =======================
       int issued_k = 0, issued_v = 0;
@@ -396,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(drain, 0, nullptr, nullptr);
     }
   } else {
-    regs_inc<kRegsSoftmax>();
+    if constexpr (L::kSplitRegs) regs_inc<L::kRegsSoftmax>();
     // ============================ softmax warpgroups ============================
     const int t = warp >> 2;              // query tile of this warpgroup
     const int row = tid & 127;            // row of the tile = tensor-memory lane
@@ -587,9 +602,9 @@ int launch_t(const PrefillArgs& a) {
   p.causal = a.causal ? 1 : 0;
   p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
   p.err = a.error_word;
-  const int pairs = (a.max_seqlen_q + pre::kRowsPerCta - 1) / pre::kRowsPerCta;
+  const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
-  kern<<<grid, pre::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
+  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill launch", e);
   return FAT_OK;
@@ -642,9 +657,9 @@ int launch_paged_t(const PrefillArgs& a) {
   p.page_size = a.page_size;
   p.rows_per_box = rpb;
   p.seq_lens_k = a.seq_lens_k;
-  const int pairs = (a.max_seqlen_q + pre::kRowsPerCta - 1) / pre::kRowsPerCta;
+  const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
-  kern<<<grid, pre::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
+  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill paged launch", e);
   return FAT_OK;
@@ -680,15 +695,21 @@ int launch_prefill_paged(const PrefillArgs& a) {
   if (!aligned16(a.out) || (a.o_st * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16 ||
       (a.o_sh * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16)
     return unsupported("prefill_paged: out must be 16-byte aligned with 16-byte-multiple strides");
-  if (a.max_seqlen_q > 65535 * pre::kRowsPerCta) return unsupported("prefill_paged: max_seqlen_q too large");
+  if (a.max_seqlen_q > 65535 * pre::BM) return unsupported("prefill_paged: max_seqlen_q too large");
+  // One producer lane per (page, 128-byte column block) of a 128-row tile.
+  if ((pre::BN / std::min(ps, pre::BN)) * (a.head_dim / 64) > 32)
+    return unsupported("prefill_paged: head_dim " + std::to_string(a.head_dim) + " needs page_size >= " +
+                       std::to_string(pre::BN * (a.head_dim / 64) / 32) + ", got " + std::to_string(ps));
   const bool bf = a.dtype == FAT_DTYPE_BF16;
   switch (a.head_dim) {
     case 64:
       return bf ? launch_paged_t<__nv_bfloat16, 64>(a) : launch_paged_t<__half, 64>(a);
     case 128:
       return bf ? launch_paged_t<__nv_bfloat16, 128>(a) : launch_paged_t<__half, 128>(a);
+    case 256:
+      return bf ? launch_paged_t<__nv_bfloat16, 256>(a) : launch_paged_t<__half, 256>(a);
     default:
-      return unsupported("prefill_paged: head_dim must be 64 or 128, got " + std::to_string(a.head_dim));
+      return unsupported("prefill_paged: head_dim must be 64, 128 or 256, got " + std::to_string(a.head_dim));
   }
 }
 
@@ -711,15 +732,17 @@ int launch_prefill_varlen(const PrefillArgs& a) {
   if (!aligned16(a.out) || (a.o_st * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16 ||
       (a.o_sh * (a.out_dtype == FAT_DTYPE_F32 ? 4 : 2)) % 16)
     return unsupported("prefill_varlen: out must be 16-byte aligned with 16-byte-multiple strides");
-  if (a.max_seqlen_q > 65535 * pre::kRowsPerCta) return unsupported("prefill_varlen: max_seqlen_q too large");
+  if (a.max_seqlen_q > 65535 * pre::BM) return unsupported("prefill_varlen: max_seqlen_q too large");
   const bool bf = a.dtype == FAT_DTYPE_BF16;
   switch (a.head_dim) {
     case 64:
       return bf ? launch_t<__nv_bfloat16, 64>(a) : launch_t<__half, 64>(a);
     case 128:
       return bf ? launch_t<__nv_bfloat16, 128>(a) : launch_t<__half, 128>(a);
+    case 256:
+      return bf ? launch_t<__nv_bfloat16, 256>(a) : launch_t<__half, 256>(a);
     default:
-      return unsupported("prefill_varlen: head_dim must be 64 or 128, got " + std::to_string(a.head_dim));
+      return unsupported("prefill_varlen: head_dim must be 64, 128 or 256, got " + std::to_string(a.head_dim));
   }
 }
 

@@ -171,7 +171,7 @@ int fat_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride
  *   out [total_q, num_heads, head_dim]   out_dtype (= dtype, or F32)
  *   cu_q, cu_k  int32 [batch + 1], non-decreasing from 0 (not checked on the device)
  *
- * head_dim in {64, 128}; all bases 16-byte aligned, token/head strides multiples
+ * head_dim in {64, 128, 256}; all bases 16-byte aligned, token/head strides multiples
  * of 16 bytes.  max_seqlen_q bounds the launch grid (queries past it are not
  * computed).  Allocates nothing.
  */
@@ -188,7 +188,7 @@ int fat_prefill_varlen(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
  * that are the last q_len of its seq_lens_k[b] cached tokens; keys and values
  * are those tokens, read from k_cache/v_cache [num_pages, page_size, num_kv_heads,
  * head_dim] through page_table [batch, max_pages] (bottom-right causal alignment:
- * query i sees key j <= i + seq_lens_k[b] - q_len).  fp16/bf16; head_dim 64 or 128;
+ * query i sees key j <= i + seq_lens_k[b] - q_len).  fp16/bf16; head_dim 64, 128 or 256 (256: page_size >= 16);
  * page_size a power of two in [8, 128] or a multiple of 128.  Rows past a
  * sequence's end never contribute; a page id outside [0, num_pages) is skipped
  * and ORs FAT_DEVERR_BAD_PAGE into *error_word.

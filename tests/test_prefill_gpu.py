@@ -77,7 +77,7 @@ def test_prefill_matches_reference_golden(name):
     assert_close_f32(out32, c["out_f32"], atol=F32_ATOL[dtype])
 
 
-@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
 @pytest.mark.parametrize("heads,kv_heads", GQA_CASES)
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -105,7 +105,7 @@ def test_prefill_zero_length_sequences_in_batch():
     _check(q, k, v, cu_q, cu_k, True, torch.float16)
 
 
-@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
 @pytest.mark.parametrize("heads,kv_heads", GQA_CASES)
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -149,3 +149,9 @@ def test_cfg3_full_size_parity(dtype):
     err = np.abs(out32.cpu().numpy() - want)
     assert err.max() <= F32_ATOL[dtype], f"max-abs {err.max():.3e}"
     assert err.mean() <= 2e-4
+
+
+def test_prefill_head_dim_256_long_and_chunked():
+    """head_dim 256 (one query tile per CTA): long causal rows and kv longer than q."""
+    q, k, v, cu_q, cu_k = varlen_case(12, [1000, 129, 3], [1000, 300, 700], 8, 2, 256, torch.bfloat16, scale=0.5)
+    _check(q, k, v, cu_q, cu_k, True, torch.bfloat16)

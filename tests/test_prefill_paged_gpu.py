@@ -82,6 +82,7 @@ CASES = [
     ([513, 128], [513, 128], 4, 4, 64, 8),               # MHA, page 8
     ([700, 260], [300, 5], 8, 1, 128, 128),              # MQA, page 128
     ([640, 1030], [640, 200], 4, 2, 128, 256),           # page larger than a tile
+    ([300, 129], [300, 40], 4, 2, 256, 16),              # head_dim 256 (one query tile per CTA)
 ]
 
 
@@ -175,3 +176,10 @@ def test_backend_decode_and_packed_prefill_routing():
     wantp = oatt.attention_varlen(to_np(qp), to_np(kp), to_np(vp), to_np(cu_q), to_np(cu_k), causal=True, scale=0.35,
                                   dtype="f16")
     assert_parity_16bit(outp, wantp, torch.float16)
+
+
+def test_paged_prefill_head_dim_256_rejects_small_pages():
+    """One producer lane per (page, column block): head_dim 256 needs 16-token pages."""
+    q, k, v, table, lens, cu_q = _case(31, [40], [40], 4, 2, 256, 8, torch.float16)
+    with pytest.raises(RuntimeError, match="page_size"):
+        _run(q, k, v, table, lens, cu_q, 8)
