@@ -280,7 +280,12 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   constexpr int kChunk = L::kChunk;
   constexpr int kTW = L::kTW;
   constexpr int NT = D / 8;  // n-tiles of the output
-  constexpr bool kBias = std::is_same<T, __half>::value && KVT == FAT_DTYPE_I8;  // biased int8 widening
+  // 8-bit caches compute in fp16 whatever the query type: codes widen to fp16
+  // exactly (int8 with a bias, e4m3 by conversion), and a bf16 query row is
+  // brought into fp16 exactly by a power-of-two scale (kQConv, below).
+  using Tc = typename std::conditional<EB == 1, __half, T>::type;
+  constexpr bool kQConv = EB == 1 && !std::is_same<T, __half>::value;
+  constexpr bool kBias = KVT == FAT_DTYPE_I8;  // biased int8 widening
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -839,6 +844,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   float m_run = -CUDART_INF_F, l_run = 0.f;
   float cs_run = 0.f;  // biased int8: running sum of the p fed to P.V (rescaled like l_run)
   float qbias = 0.f;   // biased int8: 1152 * sum(q) of row g
+  float qmul = 1.f;    // bf16 queries with 8-bit caches: the power of two the row was scaled by
   uint32_t qa[D / 16][2];
   int it = 0;
   int ev = 0;  // pieces handed to the merge warp
@@ -867,13 +873,44 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         qa[ks][0] = *reinterpret_cast<const uint32_t*>(qs + g * D + d0);
         qa[ks][1] = *reinterpret_cast<const uint32_t*>(qs + g * D + d1);
       }
-      if constexpr (kBias) {
-        float sq = 0.f;
+      if constexpr (kQConv) {
+        // Scale the row by the power of two that puts its largest magnitude in
+        // [2^14, 2^15): multiplying by it is exact, and so is the bf16 -> fp16
+        // conversion of every element that stays above fp16's normal minimum
+        // (those below are 2^-28 of the largest and vanish in the dot product).
+        // The power of two goes back into the score multiplier; |e| <= 126 keeps
+        // both 2^e and 2^-e normal floats, and covers every finite bf16 row.
+        float mx = 0.f;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           float x0, x1, x2, x3;
           unpack2<T>(qa[ks][0], x0, x1);
           unpack2<T>(qa[ks][1], x2, x3);
+          mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3))));
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        int e = 0;
+        if (mx > 0.f && mx < CUDART_INF_F) e = max(-126, min(126, ((__float_as_int(mx) >> 23) & 0xFF) - 127 - 14));
+        const float down = __int_as_float((127 - e) << 23);
+        qmul = __int_as_float((127 + e) << 23);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float x0, x1;
+            unpack2<T>(qa[ks][h], x0, x1);
+            qa[ks][h] = pack2<__half>(x0 * down, x1 * down);
+          }
+        }
+      }
+      if constexpr (kBias) {
+        float sq = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          float x0, x1, x2, x3;
+          unpack2<Tc>(qa[ks][0], x0, x1);
+          unpack2<Tc>(qa[ks][1], x2, x3);
           sq += (x0 + x1) + (x2 + x3);
         }
         sq += __shfl_xor_sync(0xffffffffu, sq, 1);
@@ -916,8 +953,8 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
           uint32_t b0, b1, b2, b3;
           ldsm_x4(L::addr(kt, row, (ks * 16 + khalf) * 2), b0, b1, b2, b3);
           const uint32_t a[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
-          MmaOp<T>::run(sacc[0], a, b0, b1);
-          MmaOp<T>::run(sacc[1], a, b2, b3);
+          MmaOp<Tc>::run(sacc[0], a, b0, b1);
+          MmaOp<Tc>::run(sacc[1], a, b2, b3);
         }
       } else {
         // 8-bit codes.  Lane (g, c) owns the reduction slice d in
@@ -948,10 +985,10 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
               if constexpr (kBias) {
                 widen_i8_biased(wv[i], b0, b1);
               } else {
-                Widen<T, KVT>::run(wv[i], b0, b1);
+                Widen<Tc, KVT>::run(wv[i], b0, b1);
               }
               const uint32_t av[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
-              MmaOp<T>::run(sacc[j], av, b0, b1);
+              MmaOp<Tc>::run(sacc[j], av, b0, b1);
             }
           }
         }
@@ -970,7 +1007,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         vsc[1] = mt.vscale[grp + 1];
       }
       // Scores in log2 units: (s - qbias) * scale * k_scale as one FMA per score.
-      const float kf[2] = {p.scale_log2 * ksc[0], p.scale_log2 * ksc[1]};
+      const float kf[2] = {p.scale_log2 * qmul * ksc[0], p.scale_log2 * qmul * ksc[1]};
       const float kb[2] = {-qbias * kf[0], -qbias * kf[1]};
       if (nvalid >= 16) {
 #pragma unroll
@@ -1003,8 +1040,8 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       // ---- O += P V : rows 0-7 carry P rounded to 16 bits, rows 8-15 the remainder ----
       uint32_t pa[4];
       const float pv[4] = {pr[0] * vsc[0], pr[1] * vsc[0], pr[2] * vsc[1], pr[3] * vsc[1]};
-      split_hi_lo<T>(pv[0], pv[1], pa[0], pa[1]);
-      split_hi_lo<T>(pv[2], pv[3], pa[2], pa[3]);
+      split_hi_lo<Tc>(pv[0], pv[1], pa[0], pa[1]);
+      split_hi_lo<Tc>(pv[2], pv[3], pa[2], pa[3]);
       if constexpr (kBias) cs_run = cs_run * alpha + ((pv[0] + pv[1]) + (pv[2] + pv[3]));
       if constexpr (EB == 2) {
         const int row = wrow + ((lane >> 3) & 1) * 8 + (lane & 7);
@@ -1013,8 +1050,8 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         for (int np = 0; np < D / 16; ++np) {
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(L::addr(vt, row, (np * 16 + dsel) * 2), b0, b1, b2, b3);
-          MmaOp<T>::run(o[2 * np], pa, b0, b1);
-          MmaOp<T>::run(o[2 * np + 1], pa, b2, b3);
+          MmaOp<Tc>::run(o[2 * np], pa, b0, b1);
+          MmaOp<Tc>::run(o[2 * np + 1], pa, b2, b3);
         }
       } else {
         // 8-bit V: lane (g, c) owns output dims [g*D/8, (g+1)*D/8) (B column g
@@ -1050,21 +1087,21 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
               const uint32_t sel = uint32_t(i) * 0x11u + uint32_t(4 + i) * 0x1100u;
               const uint32_t b0 = biased_pair_i8(__byte_perm(rw[0][w], rw[1][w], sel));
               const uint32_t b1 = biased_pair_i8(__byte_perm(rw[2][w], rw[3][w], sel));
-              MmaOp<T>::run(o[4 * w + i], pa, b0, b1);
+              MmaOp<Tc>::run(o[4 * w + i], pa, b0, b1);
             }
           }
         } else {
 #pragma unroll
         for (int w = 0; w < kSlice / 4; ++w) {
           uint32_t b0a, b0b, b0c, b0d, b1a, b1b, b1c, b1d;
-          Widen<T, KVT>::run(__byte_perm(rw[0][w], rw[1][w], 0x5140), b0a, b0b);
-          Widen<T, KVT>::run(__byte_perm(rw[0][w], rw[1][w], 0x7362), b0c, b0d);
-          Widen<T, KVT>::run(__byte_perm(rw[2][w], rw[3][w], 0x5140), b1a, b1b);
-          Widen<T, KVT>::run(__byte_perm(rw[2][w], rw[3][w], 0x7362), b1c, b1d);
-          MmaOp<T>::run(o[4 * w + 0], pa, b0a, b1a);
-          MmaOp<T>::run(o[4 * w + 1], pa, b0b, b1b);
-          MmaOp<T>::run(o[4 * w + 2], pa, b0c, b1c);
-          MmaOp<T>::run(o[4 * w + 3], pa, b0d, b1d);
+          Widen<Tc, KVT>::run(__byte_perm(rw[0][w], rw[1][w], 0x5140), b0a, b0b);
+          Widen<Tc, KVT>::run(__byte_perm(rw[0][w], rw[1][w], 0x7362), b0c, b0d);
+          Widen<Tc, KVT>::run(__byte_perm(rw[2][w], rw[3][w], 0x5140), b1a, b1b);
+          Widen<Tc, KVT>::run(__byte_perm(rw[2][w], rw[3][w], 0x7362), b1c, b1d);
+          MmaOp<Tc>::run(o[4 * w + 0], pa, b0a, b1a);
+          MmaOp<Tc>::run(o[4 * w + 1], pa, b0b, b1b);
+          MmaOp<Tc>::run(o[4 * w + 2], pa, b0c, b1c);
+          MmaOp<Tc>::run(o[4 * w + 3], pa, b0d, b1d);
         }
         }
       }

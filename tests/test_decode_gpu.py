@@ -220,6 +220,35 @@ def test_quantised_decode_matches_dequantised_oracle(mode, dtype, head_dim, page
     assert worst <= (1.2e-2 if dtype == torch.bfloat16 else 2e-3)
 
 
+@pytest.mark.parametrize("mode", ["int8", "float8_e4m3fn"])
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
+def test_quantised_decode_bf16_query_rows_of_extreme_magnitude(mode, head_dim):
+    """8-bit caches compute in fp16 for bf16 queries too: each query row is
+    scaled by a power of two into fp16's range. Rows far outside fp16's range
+    (1e30, 1e-30), mixed-magnitude rows and zero rows must come out as the
+    fp32 oracle on the same bf16 queries and dequantised cache does."""
+    ps = 16
+    lens = [33, 300, 1000]
+    q, k, v, table, lens = paged_case(29, lens, 8, 2, head_dim, ps, torch.float32)
+    q = q * 0.05  # keep the 1e4 row's softmax from collapsing onto one token
+    gains = [1e4, 1e-6, 1e30, 1e-30, 1.0, 0.0, 3e-3, 1e2]
+    for h, gain in enumerate(gains):
+        q[:, h] *= gain
+    q[:, 4, ::2] *= 1e3  # mixed magnitudes within one row
+    qb = q.to(torch.bfloat16)
+    qk, qv, sk, sv = oquant.quantize_kv_pages(k.numpy(), v.numpy(), mode)
+    tdt = torch.int8 if mode == "int8" else torch.float8_e4m3fn
+    out32 = _run(qb, from_np(qk, tdt), from_np(qv, tdt), table, lens, ps, out_dtype=torch.float32,
+                 k_scale=torch.from_numpy(sk), v_scale=torch.from_numpy(sv))
+    dk, dv = oquant.dequantize_kv_pages(qk, qv, sk, sv, mode)
+    want = oatt.attention_paged(qb.float().numpy(), dk.astype(np.float32), dv.astype(np.float32), to_np(table),
+                                to_np(lens), ps, dtype="f32", out_f32=True)
+    assert np.isfinite(to_np(out32)).all()
+    worst = assert_close_f32(out32, want, atol=ATOL_QUANT)
+    assert worst <= 2e-3
+    _no_device_error()
+
+
 def test_quantised_op_and_golden():
     import flashattntile_b200  # noqa: F401
 
