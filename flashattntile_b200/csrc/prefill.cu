@@ -56,6 +56,7 @@ struct Params {
   float scale_log2;
   int causal;
   int out_f32;
+  int o_tma;             // tm_o describes out (16-bit output): full 32-row groups leave by TMA stores
   int* err;
   // Paged K/V (kPaged): sequence b's keys are its seq_lens_k[b] cached tokens.
   const int* page_table;
@@ -125,7 +126,8 @@ __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int c
 template <typename T, int D, bool kPaged>
 __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                   const Params p) {
   using L = Layout<D>;
   constexpr int SK = L::kStagesK, SV = L::kStagesV;
   constexpr int kTiles = L::kTiles, kRowsPerCta = L::kRowsPerCta;
@@ -505,7 +507,50 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       mbar_arrive(pbar);
     }
     // ---- epilogue: O / l -> global, once the last P.V of this tile completed ----
-    if (ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag)) {
+    const bool fin = ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag);
+    // A warp whose 32 rows all belong to the sequence stages them, 16-bit and
+    // 128-byte swizzled, in its rows of the tile's Q buffer (unused once the
+    // tile's last MMA completed) and stores them with one TMA copy per 64
+    // columns: whole 128-byte lines leave instead of each store instruction
+    // touching 32 rows' lines with 16 bytes.  Rows of a partial group (the
+    // next sequence's rows follow in out) take the direct stores below.
+    const int wrow0 = m0 + t * BM + 32 * (warp & 3);
+    if (p.o_tma && n_t > 0 && wrow0 + 32 <= q_len) {
+      if (__all_sync(0xffffffffu, fin)) {
+        tc::fence_after_sync();
+        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        const uint32_t qt = sQ + uint32_t(t * L::kTile);
+#pragma unroll
+        for (int c = 0; c < D / 32; c += 2) {
+          uint32_t r[2][32];
+          tc::ld32(lane_base + colO + 32 * c, r[0]);
+          tc::ld32(lane_base + colO + 32 * (c + 1), r[1]);
+          tc::wait_ld();
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const uint32_t blk = qt + uint32_t(((c + u) >> 1) * BM * 128);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t* x = r[u] + 8 * i;
+              st_shared_v4(blk + swz128(uint32_t(row), uint32_t(((c + u) & 1) * 4 + i)),
+                           pack2<T>(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
+                           pack2<T>(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
+                           pack2<T>(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
+                           pack2<T>(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int cb = 0; cb < L::kCB; ++cb)
+            tma_store_3d(&tm_o, qt + uint32_t(cb * BM * 128 + (warp & 3) * 32 * 128), cb * 64, h, q0 + wrow0);
+          bulk_commit_group();
+          bulk_wait_read_all();
+        }
+      }
+    } else if (fin) {
       tc::fence_after_sync();
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
       const bool store = q_idx < q_len;
@@ -562,6 +607,25 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
 // =============================================================================
 namespace {
 
+// Map of the 16-bit output {head_dim, head, token} in 64-column, 32-row boxes
+// (the epilogue's TMA stores).  fp32 output, or a layout the map cannot
+// describe, keeps the direct stores (the map is then a placeholder).
+template <int D>
+int encode_out_map(const PrefillArgs& a, const CUtensorMap& placeholder, CUtensorMap* to) {
+  *to = placeholder;
+  if (a.out_dtype == FAT_DTYPE_F32) return 0;
+  std::string why;
+  const uint32_t box[3] = {64u, 1u, 32u};
+  const uint64_t dims[3] = {uint64_t(D), uint64_t(a.num_heads), uint64_t(a.total_q)};
+  const uint64_t strides[2] = {uint64_t(a.o_sh) * 2, uint64_t(a.o_st) * 2};
+  if (!encode_tiled(to, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                    &why)) {
+    *to = placeholder;
+    return 0;
+  }
+  return 1;
+}
+
 template <typename T, int D>
 int launch_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
@@ -591,6 +655,8 @@ int launch_t(const PrefillArgs& a) {
       return invalid("prefill v: " + why);
   }
   pre::Params p{};
+  CUtensorMap to;
+  p.o_tma = encode_out_map<D>(a, tq, &to);
   p.cu_q = a.cu_q;
   p.cu_k = a.cu_k;
   p.out = a.out;
@@ -604,7 +670,7 @@ int launch_t(const PrefillArgs& a) {
   p.err = a.error_word;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
-  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
+  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill launch", e);
   return FAT_OK;
@@ -640,6 +706,8 @@ int launch_paged_t(const PrefillArgs& a) {
       return invalid("prefill v_cache: " + why);
   }
   pre::Params p{};
+  CUtensorMap to;
+  p.o_tma = encode_out_map<D>(a, tq, &to);
   p.cu_q = a.cu_q;
   p.out = a.out;
   p.o_st = a.o_st;
@@ -659,7 +727,7 @@ int launch_paged_t(const PrefillArgs& a) {
   p.seq_lens_k = a.seq_lens_k;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
-  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, p);
+  kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill paged launch", e);
   return FAT_OK;
