@@ -240,10 +240,13 @@ int fat_gather_paged(const void* k_cache, const void* v_cache, int64_t stride_pa
  * flashattn_tile/paging.py:84-130 (validate_cache): host_out[0..3] = min and max
  * of seq_lens[batch], then min and max of the page-table entries a sequence of
  * the maximum length reaches (the first ceil(max / page_size) columns of every
- * row, at most max_pages; (0, -1) when there are none).  Queues one kernel and
- * a 16-byte copy into host_out (host memory, pinned for an asynchronous copy)
- * on `stream`; synchronise the stream (or an event recorded after this call)
- * before reading host_out.  device_scratch: 4 int32 on the device.  Replaces
+ * row, at most max_pages; (0, -1) when there are none).  Queues one kernel on
+ * `stream`: when host_out is pinned host memory mapped into the device's
+ * address space (cudaHostAlloc / cudaHostRegister memory, 16-byte aligned) the
+ * kernel writes it directly, otherwise it writes device_scratch and a 16-byte
+ * copy into host_out follows.  Synchronise the stream (or an event recorded
+ * after this call) before reading host_out.  device_scratch: 4 int32 on the
+ * device (unused when host_out is written directly).  Replaces
  * the reference's torch reductions + read-back of both tensors.
  */
 int fat_cache_value_stats(const int32_t* seq_lens, const int32_t* page_table, int64_t page_table_stride, int batch,

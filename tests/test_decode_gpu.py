@@ -377,6 +377,41 @@ def test_cache_value_stats_kernel_matches_torch(case):
     assert got == _torch_value_stats(lens, table, ps)
 
 
+@pytest.mark.parametrize("host_kind", ["pinned", "pageable"])
+@pytest.mark.parametrize("scratch_offset", [0, 4])
+def test_cache_value_stats_host_buffers(host_kind, scratch_offset):
+    """The C ABI writes pinned (device-mapped) host memory from the kernel and
+    copies into pageable memory; a device scratch that is only 4-byte aligned
+    is written element by element.  Both give the torch reductions' numbers."""
+    import ctypes
+
+    from flashattntile_b200 import _lib
+
+    gen = torch.Generator().manual_seed(77)
+    batch, max_pages, ps = 41, 70, 16
+    table = torch.randint(0, 9000, (batch, max_pages), generator=gen, dtype=torch.int32)
+    lens = torch.randint(1, max_pages * ps, (batch,), generator=gen, dtype=torch.int32)
+    want = _torch_value_stats(lens, table, ps)
+    lens_d, table_d = lens.to(DEV), table.to(DEV)
+    scratch = torch.zeros(8, dtype=torch.int32, device=DEV)
+    if host_kind == "pinned":
+        host = torch.full((4,), -99, dtype=torch.int32).pin_memory()
+        host_ptr = host.data_ptr()
+    else:
+        host_np = np.full(4, -99, dtype=np.int32)
+        host_ptr = host_np.ctypes.data
+    stream = torch.cuda.current_stream()
+    status = _lib.load().fat_cache_value_stats(lens_d.data_ptr(), table_d.data_ptr(), table_d.stride(0), batch,
+                                               max_pages, ps, scratch.data_ptr() + scratch_offset,
+                                               ctypes.c_void_p(host_ptr), stream.cuda_stream)
+    assert status == 0
+    stream.synchronize()
+    got = host.tolist() if host_kind == "pinned" else host_np.tolist()
+    assert got == want
+    if host_kind == "pageable":  # the copy path went through the scratch words
+        assert scratch.cpu()[scratch_offset // 4:scratch_offset // 4 + 4].tolist() == want
+
+
 def test_validation_errors_raised_through_the_stats_kernel():
     """The op's value checks (reference messages) still fire with the kernel path."""
     from flashattntile_b200.paging import validate_cache
