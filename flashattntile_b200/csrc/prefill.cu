@@ -103,6 +103,29 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
+// Two-lane fp32 arithmetic (sm_100a FFMA2 / FADD2): one issue slot for two
+// independent round-to-nearest operations, each lane bitwise equal to the
+// scalar fmaf / add.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 rs, ra;\n\t"
+      "mov.b64 rs, {%0, %1};\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\t"
+      "mov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+
 template <int Regs>
 __device__ __forceinline__ void regs_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Regs));
@@ -488,14 +511,15 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         uint32_t packed[32];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = fast_exp2(fmaf(s[64 * c + 2 * i], p.scale_log2, -msub));
-          const float p1 = fast_exp2(fmaf(s[64 * c + 2 * i + 1], p.scale_log2, -msub));
-          const float p2 = fast_exp2(fmaf(s[64 * c + 2 * i + 2], p.scale_log2, -msub));
-          const float p3 = fast_exp2(fmaf(s[64 * c + 2 * i + 3], p.scale_log2, -msub));
-          sum0 += p0;
-          sum1 += p1;
-          sum2 += p2;
-          sum3 += p3;
+          float x0, x1, x2, x3;
+          fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
+          fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
+          const float p0 = fast_exp2(x0);
+          const float p1 = fast_exp2(x1);
+          const float p2 = fast_exp2(x2);
+          const float p3 = fast_exp2(x3);
+          add2(sum0, sum1, p0, p1);
+          add2(sum2, sum3, p2, p3);
           packed[i] = pack2<T>(p0, p1);
           packed[i + 1] = pack2<T>(p2, p3);
         }
