@@ -473,9 +473,11 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       }
       float mx;
       {
-        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+        // Four independent chains over the BN scores: blocks of 8 from 0.
+        static_assert(BN % 8 == 0, "row max works on blocks of 8 scores");
+        float a0 = fmaxf(s[0], s[4]), a1 = fmaxf(s[1], s[5]), a2 = fmaxf(s[2], s[6]), a3 = fmaxf(s[3], s[7]);
 #pragma unroll
-        for (int i = 4; i < BN; i += 8) {
+        for (int i = 8; i < BN; i += 8) {
           a0 = max3(a0, s[i], s[i + 4]);
           a1 = max3(a1, s[i + 1], s[i + 5]);
           a2 = max3(a2, s[i + 2], s[i + 6]);
