@@ -47,6 +47,7 @@ constexpr int kMaxChunk = 256;             // largest chunk (tokens per pipeline
 constexpr int kMaxBoxes = 32;              // TMA row boxes per chunk at most (chunk / 8)
 constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
 constexpr size_t kSmemMax = 227 * 1024;    // shared memory per CTA (opt-in maximum)
+constexpr float kDecodeRescaleLog2 = 8.f;  // running-max slack before O is rescaled (P <= 2^8)
 
 enum : int { kFirst = 1, kLast = 2, kFull = 4, kDone = 8 };
 
@@ -1020,7 +1021,10 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run, mx);
+      // The running max moves only when a score exceeds it by more than 2^8
+      // (log2 units), so P stays <= 256 and O is rescaled rarely; o, l and m
+      // stay consistent, so the fold and the log-sum-exp merge are unchanged.
+      const float m_new = (mx > m_run + kDecodeRescaleLog2) ? mx : m_run;
       const float alpha = fast_exp2(m_run - m_new);
       float pr[4];
 #pragma unroll
