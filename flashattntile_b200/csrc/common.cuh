@@ -284,6 +284,38 @@ __device__ __forceinline__ void split_hi_lo(float p0, float p1, uint32_t& hi, ui
   lo = pack2<T>(p0 - h0, p1 - h1);
 }
 
+// Two-lane fp32 arithmetic (sm_100a FFMA2 / FADD2 / FMUL2): one issue slot for
+// two independent round-to-nearest operations, each lane bitwise equal to the
+// scalar fmaf / add / mul (no flush to zero, like the scalar code here).
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 rs, ra;\n\t"
+      "mov.b64 rs, {%0, %1};\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\t"
+      "mov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

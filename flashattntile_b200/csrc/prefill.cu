@@ -103,29 +103,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-// Two-lane fp32 arithmetic (sm_100a FFMA2 / FADD2): one issue slot for two
-// independent round-to-nearest operations, each lane bitwise equal to the
-// scalar fmaf / add.
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "mov.b64 rb, {%4, %4};\n\t"
-      "mov.b64 rc, {%5, %5};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
-      "mov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b), "f"(c));
-}
-__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
-  asm("{\n\t.reg .b64 rs, ra;\n\t"
-      "mov.b64 rs, {%0, %1};\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "add.rn.f32x2 rs, rs, ra;\n\t"
-      "mov.b64 {%0, %1}, rs;\n\t}"
-      : "+f"(s0), "+f"(s1)
-      : "f"(a0), "f"(a1));
-}
-
 template <int Regs>
 __device__ __forceinline__ void regs_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Regs));
