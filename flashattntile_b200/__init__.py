@@ -29,6 +29,8 @@ def device_error(device: torch.device | str | int | None = None) -> int:
 
     Bit 1 (``FAT_DEVERR_TIMEOUT``): a bounded in-kernel wait gave up.
     Bit 2 (``FAT_DEVERR_BAD_PAGE``): a page id outside the cache was skipped.
+    Bit 4 (``FAT_DEVERR_BAD_LENGTH``): a sequence length beyond the page table's
+    capacity (``max_pages * page_size``) was cut to that capacity.
     """
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     if dev.type == "cuda" and dev.index is None:

@@ -29,6 +29,7 @@ FAT_ERR_WORKSPACE = 4
 
 FAT_DEVERR_TIMEOUT = 1
 FAT_DEVERR_BAD_PAGE = 2
+FAT_DEVERR_BAD_LENGTH = 4
 
 DTYPE_CODE = {
     torch.float16: 0,
@@ -49,6 +50,8 @@ _sz = ctypes.c_size_t
 SIGNATURES: dict[str, tuple] = {
     "fat_version": (ctypes.c_char_p, []),
     "fat_last_error": (ctypes.c_char_p, []),
+    "fat_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
+    "fat_expire_next_waits": (None, [_i32]),
     "fat_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "fat_paged_decode": (
         _i32,

@@ -17,6 +17,10 @@ const char* fat_version(void) { return "flashattn_tile_b200 0.1.0 sm_100a"; }
 
 const char* fat_last_error(void) { return fat::last_error(); }
 
+uint64_t fat_set_wait_limit_ns(uint64_t limit_ns) { return fat::set_wait_limit_ns(limit_ns); }
+
+void fat_expire_next_waits(int launches) { fat::request_expiry(launches); }
+
 size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int num_kv_heads, int head_dim) {
   return fat::decode_workspace_bytes(device, batch, num_heads, num_kv_heads, head_dim);
 }

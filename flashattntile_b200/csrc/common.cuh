@@ -19,8 +19,9 @@ namespace fat {
 // ---------------------------------------------------------------------------
 // Error word and bounded waits
 // ---------------------------------------------------------------------------
-// Every spin in these kernels gives up after kWaitLimitNs of wall time (the
-// %globaltimer register), records FAT_DEVERR_TIMEOUT in the caller's error
+// Every spin in these kernels gives up after a limit of wall time (the
+// %globaltimer register; kWaitLimitNs unless the launch passes another,
+// fat_set_wait_limit_ns), records FAT_DEVERR_TIMEOUT in the caller's error
 // word and lets the kernel unwind instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
@@ -88,9 +89,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar` to complete; false (and the error word set)
-// if it did not within kWaitLimitNs or if `abort` (shared flag) was raised.
+// if it did not within `limit_ns` or if `abort` (shared flag) was raised.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int* err,
-                                                  volatile int* abort) {
+                                                  volatile int* abort, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t polls = 0;
@@ -98,7 +99,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((++polls & 63u) == 0u) {
       if (abort != nullptr && *abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         raise_error(err, FAT_DEVERR_TIMEOUT);
         if (abort != nullptr) *abort = 1;
         return false;

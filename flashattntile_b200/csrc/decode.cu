@@ -33,6 +33,8 @@
 // FAT_DEVERR_TIMEOUT, drains its own TMA copies and returns.
 #include <math_constants.h>
 
+#include <algorithm>
+
 #include <type_traits>
 
 #include "common.cuh"
@@ -44,6 +46,7 @@ namespace dec {
 
 constexpr int kProducers = 2;              // producer warps (take turns by chunk)
 constexpr int kMaxChunk = 256;             // largest chunk (tokens per pipeline stage) of any layout
+constexpr int kMaxTokens = 1 << 30;        // longest sequence the kernel walks (positions stay far below 2^31)
 constexpr int kMaxBoxes = 32;              // TMA row boxes per chunk at most (chunk / 8)
 constexpr int kRows = 8;                   // query heads per unit (M rows 0-7; 8-15 carry P remainders)
 constexpr size_t kSmemMax = 227 * 1024;    // shared memory per CTA (opt-in maximum)
@@ -101,6 +104,7 @@ struct Params {
   const float* v_scale;
   long long s_sp;  // scale stride per page (head stride 1)
   int batch, num_heads, num_kv_heads, group, head_groups, page_size, num_pages, box_rows, max_pages;
+  int cap_tokens;  // min(max_pages * page_size, kMaxTokens): every length is cut to this
   float scale_log2;
   int out_f32;
   float* lse;    // optional [batch][num_heads] (stride lse_sb): m + log2(l), base-2 log-sum-exp
@@ -109,6 +113,8 @@ struct Params {
   float* ws_ml;  // [grid][2][kRows][2]
   int* ws_count; // [units]
   int* err;
+  unsigned long long wait_ns;  // limit of every bounded wait
+  int expire;    // consumer warp 0 first waits on a barrier phase nothing completes (failure-path tests)
 };
 
 template <int D, int EB>
@@ -176,6 +182,15 @@ struct Split {
     return narrow ? int((uint32_t(x + 1) * uint32_t(nc) - 1u) / uint32_t(total)) : int(((x + 1) * nc - 1) / total);
   }
 };
+
+// Cached tokens of sequence b as the kernel walks them: a negative length
+// counts as 0, a length past the page table (max_pages * page_size, at most
+// kMaxTokens) is cut to it, so no token position, chunk count or page index
+// derived from it can overflow 32 bits or leave the table.  The cut is
+// reported (FAT_DEVERR_BAD_LENGTH) once per sequence by the zero-row pass.
+__device__ __forceinline__ int seq_len_of(const Params& p, int b) {
+  return min(max(__ldg(p.seq_lens + b), 0), p.cap_tokens);
+}
 
 // ---------------------------------------------------------------------------
 // 8-bit KV codes -> 16-bit MMA operands, exactly (every int8 and every finite
@@ -298,7 +313,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   float* mM = mO + kWarps * kRows * (D + 8);
   float* mL = mM + kWarps * kRows;
   uint64_t* bars = reinterpret_cast<uint64_t*>(mL + kWarps * kRows);
-  volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 2);  // [0] abort
+  volatile int* shi = reinterpret_cast<volatile int*>(bars + 2 * kStages + 2);  // [0] abort, [2..3] `never`
   long long* shl = reinterpret_cast<long long*>(const_cast<int*>(shi) + 4);   // [0] start_b [1] start_S [2] total
   volatile MergeEvent* evt = reinterpret_cast<volatile MergeEvent*>(shl + 4);
   long long* scan = reinterpret_cast<long long*>(stages);  // [kThreads + kThreads / 32], prologue only
@@ -312,6 +327,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   const uint32_t empty0 = full0 + 8u * kStages;
   const uint32_t mfull = full0 + 16u * kStages;  // consumer warps -> merge warp: a piece is in the merge area
   const uint32_t mfree = mfull + 8u;             // merge warp -> consumer warps: the merge area is free
+  const uint32_t never = smem_u32(const_cast<int*>(shi) + 2);  // initialised, never arrived on
   const int nkg = p.num_kv_heads * p.head_groups;
 
   if (tid == 0) {
@@ -321,6 +337,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     }
     mbar_init(mfull, kWarps * 32);
     mbar_init(mfree, 1);
+    mbar_init(never, 1);
     shi[0] = 0;
     shl[0] = -1;
     fence_barrier_init();
@@ -332,7 +349,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     const int b0 = tid * per;
     const int b1 = min(p.batch, b0 + per);
     long long mine = 0;
-    for (int b = b0; b < b1; ++b) mine += (max(__ldg(p.seq_lens + b), 0) + kChunk - 1) / kChunk;
+    for (int b = b0; b < b1; ++b) mine += (seq_len_of(p, b) + kChunk - 1) / kChunk;
     // Exclusive prefix sum of `mine` over the block: warp scans, then a scan
     // of the warp totals by warp 0 (a serial loop here cost microseconds).
     long long* wsum = scan + kThreads;  // [kThreads / 32]
@@ -363,7 +380,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     if (x0 < total && pre <= x0 && x0 < pre + mine * nkg) {
       long long s = scan[tid];
       for (int b = b0; b < b1; ++b) {
-        const long long cb = (max(__ldg(p.seq_lens + b), 0) + kChunk - 1) / kChunk;
+        const long long cb = (seq_len_of(p, b) + kChunk - 1) / kChunk;
         if (x0 < (s + cb) * nkg) {
           shl[0] = b;
           shl[1] = s;
@@ -381,7 +398,9 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
 
   // Sequences without cached tokens own no chunks: their output rows are zero.
   for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
-    if (__ldg(p.seq_lens + b) > 0) continue;
+    const int raw_len = __ldg(p.seq_lens + b);
+    if (raw_len > p.cap_tokens && tid == 0) raise_error(p.err, FAT_DEVERR_BAD_LENGTH);
+    if (raw_len > 0) continue;
     for (int idx = tid; idx < p.num_heads * D; idx += kThreads) {
       const int h = idx / D, d = idx - h * D;
       const long long off = (long long)b * p.o_sb + (long long)h * p.o_sh + d;
@@ -424,7 +443,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
       // no 64-bit division (emulated and slow on the GPU).
       int wb = int(shl[0]);
       long long wS = shl[1];
-      int wlen = max(__ldg(p.seq_lens + wb), 0);
+      int wlen = seq_len_of(p, wb);
       int wchunks = (wlen + kChunk - 1) / kChunk;
       int wunit, wchunk;
       {
@@ -442,7 +461,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
             wS += wchunks;
             do {
               ++wb;
-              wlen = max(__ldg(p.seq_lens + wb), 0);
+              wlen = seq_len_of(p, wb);
               wchunks = (wlen + kChunk - 1) / kChunk;
             } while (wchunks == 0 && wb + 1 < p.batch);
           }
@@ -469,7 +488,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
           if (lane < nbox) {
             const int lp = (tok0 + lane * p.box_rows) / p.page_size;
             int* dst = rids + r * kMaxBoxes + lane;
-            if (lp < p.max_pages) {
+            if (lp >= 0 && lp < p.max_pages) {
               cp_async_4(smem_u32(dst), p.page_table + (long long)wb * p.pt_sb + lp);
             } else {
               *dst = -1;
@@ -525,7 +544,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
         const bool full_seg = (i - chunk >= 0) && (i - chunk + chunks_b <= n);
         const int s = i % kStages;
         const uint32_t parity = uint32_t(((i / kStages) & 1) ^ 1);
-        if (!mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) break;
+        if (!mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag, p.wait_ns)) break;
 
         const int kvh = unit_local / p.head_groups;
         const int hg = unit_local - kvh * p.head_groups;
@@ -611,7 +630,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     if (!*abort_flag && n % kProducers == pid) {
       const int s = n % kStages;
       const uint32_t parity = uint32_t(((n / kStages) & 1) ^ 1);
-      if (mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag)) {
+      if (mbar_wait_bounded(empty0 + 8u * s, parity, p.err, abort_flag, p.wait_ns)) {
         if (lane == 0) {
           meta[s].flags = kDone;
           mbar_arrive(full0 + 8u * s);
@@ -621,7 +640,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     if (*abort_flag && lane == 0) {
       for (int j = max(0, own_issued - kStages); j < own_issued; ++j) {
         const int i = pid + j * kProducers;
-        mbar_wait_bounded(full0 + 8u * (i % kStages), uint32_t((i / kStages) & 1), nullptr, nullptr);
+        mbar_wait_bounded(full0 + 8u * (i % kStages), uint32_t((i / kStages) & 1), nullptr, nullptr, p.wait_ns);
       }
     }
     return;
@@ -695,7 +714,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     const Split split(total, gridDim.x);
     int ev = 0;
     while (true) {
-      if (!mbar_wait_bounded(mfull, uint32_t(ev & 1), p.err, abort_flag)) break;
+      if (!mbar_wait_bounded(mfull, uint32_t(ev & 1), p.err, abort_flag, p.wait_ns)) break;
       const int flags = evt->flags;
       if (flags & kDone) break;
       const int b = evt->b, unit_local = evt->unit_local, chunks_b = evt->chunks_b;
@@ -849,10 +868,14 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   uint32_t qa[D / 16][2];
   int it = 0;
   int ev = 0;  // pieces handed to the merge warp
+  // Failure-path test: a wait that nothing ends runs out after p.wait_ns,
+  // records FAT_DEVERR_TIMEOUT and raises the abort flag; every other warp
+  // then stops at its next wait and drains its copies.
+  if (p.expire && warp == 0) mbar_wait_bounded(never, 0, p.err, abort_flag, p.wait_ns);
 
   while (true) {
     const int s = it % kStages;
-    if (!mbar_wait_bounded(full0 + 8u * s, uint32_t((it / kStages) & 1), p.err, abort_flag)) break;
+    if (!mbar_wait_bounded(full0 + 8u * s, uint32_t((it / kStages) & 1), p.err, abort_flag, p.wait_ns)) break;
     const Meta& mt = meta[s];
     const int flags = mt.flags;
     if (flags & kDone) break;
@@ -1135,7 +1158,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
     if (flags & kLast) {
       // ---- end of this CTA's piece of a unit: hand the warps' partials to
       // the merge warp (once it has taken the previous piece) and go on ----
-      if (ev > 0 && !mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag)) break;
+      if (ev > 0 && !mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag, p.wait_ns)) break;
       const float l_row = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
       const float l_tot = l_row + __shfl_xor_sync(0xffffffffu, l_row, 2);
       float corr = 0.f;  // biased int8: 1152 * sum(p) of row g over the piece
@@ -1170,7 +1193,7 @@ __global__ void __launch_bounds__(Layout<D, elem_bytes<KVT>()>::kThreads, 1)
   }
   // No more pieces: tell the merge warp (after it has taken the last one).
   // After an abort it stops on the shared abort flag instead.
-  if (!*abort_flag && (ev == 0 || mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag))) {
+  if (!*abort_flag && (ev == 0 || mbar_wait_bounded(mfree, uint32_t((ev - 1) & 1), p.err, abort_flag, p.wait_ns))) {
     if (ctid == 0) evt->flags = kDone;
     mbar_arrive(mfull);
   }
@@ -1243,6 +1266,7 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   p.page_table = a.page_table;
   p.pt_sb = a.pt_sb;
   p.max_pages = int(a.max_pages);
+  p.cap_tokens = int(std::min<long long>((long long)a.max_pages * a.page_size, dec::kMaxTokens));
   p.seq_lens = a.seq_lens;
   p.k_scale = a.k_scale;
   p.v_scale = a.v_scale;
@@ -1264,6 +1288,8 @@ int launch_t(const DecodeArgs& a, int device, int grid, const WsLayout& ws) {
   p.err = a.error_word;
   p.lse = a.lse;
   p.lse_sb = a.lse_sb;
+  p.wait_ns = wait_limit_ns();
+  p.expire = take_expire_request() ? 1 : 0;
   (void)device;
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tmk, tmv, p);
   e = cudaGetLastError();
@@ -1309,7 +1335,7 @@ void decode_ticket_range(int device, int batch, int num_heads, int num_kv_heads,
   *bytes = size_t(units) * sizeof(int);
 }
 
-int launch_paged_decode(const DecodeArgs& a) {
+int check_paged_decode(const DecodeArgs& a) {
   if (a.batch < 0) return invalid("paged_decode: batch must be non-negative");
   if (a.num_heads <= 0 || a.num_kv_heads <= 0) return invalid("paged_decode: head counts must be positive");
   if (a.num_heads % a.num_kv_heads != 0)
@@ -1339,7 +1365,14 @@ int launch_paged_decode(const DecodeArgs& a) {
     return unsupported("paged_decode: K/V base addresses and page/slot/head strides must be 16-byte aligned");
   if (!aligned16(a.q) || (a.q_sb * 2) % 16 || (a.q_sh * 2) % 16)
     return unsupported("paged_decode: q must be 16-byte aligned with 16-byte-multiple strides");
+  if (a.head_dim != 32 && a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256)
+    return unsupported("paged_decode: head_dim must be 32, 64, 128 or 256, got " + std::to_string(a.head_dim));
+  return FAT_OK;
+}
 
+int launch_paged_decode(const DecodeArgs& a) {
+  const int rc = check_paged_decode(a);
+  if (rc != FAT_OK || a.batch == 0) return rc;
   const int device = current_device();
   const int grid = sm_count(device);
   const int group = a.num_heads / a.num_kv_heads;
@@ -1351,6 +1384,7 @@ int launch_paged_decode(const DecodeArgs& a) {
                    std::to_string(ws.total));
     return FAT_ERR_WORKSPACE;
   }
+  if (device < 0) return invalid("paged_decode: no current CUDA device");
 
   if (a.q_dtype == FAT_DTYPE_F16) {
     switch (a.kv_dtype) {

@@ -41,6 +41,10 @@ size_t decode_workspace_bytes(int device, int batch, int num_heads, int num_kv_h
 void decode_ticket_range(int device, int batch, int num_heads, int num_kv_heads, int head_dim, size_t* offset,
                          size_t* bytes);
 
+// Every argument check of launch_paged_decode except the workspace size (no
+// GPU work, no CUDA call). Returns a fat_status.
+int check_paged_decode(const DecodeArgs& a);
+
 // Validate, build the TMA descriptors and launch. Returns a fat_status.
 int launch_paged_decode(const DecodeArgs& a);
 

@@ -76,14 +76,6 @@ extern "C" int fat_paged_decode_noalloc(
   void* scratch = nullptr;
   int rc = fat::scratch_address(device, &scratch);
   if (rc != FAT_OK) return rc;
-  // The per-unit tickets must start at zero.  A completed call leaves them
-  // zero, but one that stopped early (a device error) may not: clear them on
-  // this call's stream first.
-  size_t off = 0, bytes = 0;
-  fat::decode_ticket_range(device, batch, num_heads, num_kv_heads, head_dim, &off, &bytes);
-  const cudaError_t e =
-      cudaMemsetAsync(static_cast<unsigned char*>(scratch) + off, 0, bytes, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return fat::cuda_failure("paged_decode_noalloc: clearing tickets", e);
 
   fat::DecodeArgs a;
   a.q = q;
@@ -118,5 +110,18 @@ extern "C" int fat_paged_decode_noalloc(
   a.workspace_bytes = fat::kNoAllocScratchBytes;
   a.error_word = error_word;
   a.stream = static_cast<cudaStream_t>(stream);
+  // A refused call queues no GPU work: every argument is checked before the
+  // ticket clear below.
+  rc = fat::check_paged_decode(a);
+  if (rc != FAT_OK) return rc;
+  // The per-unit tickets must start at zero.  A completed call leaves them
+  // zero, but one that stopped early (a device error) may not, and nothing on
+  // the host knows without a synchronisation: clear them on this call's stream
+  // (a memset node of 4 bytes per unit, ~2 us of GPU time, ahead of the kernel).
+  size_t off = 0, bytes = 0;
+  fat::decode_ticket_range(device, batch, num_heads, num_kv_heads, head_dim, &off, &bytes);
+  const cudaError_t e =
+      cudaMemsetAsync(static_cast<unsigned char*>(scratch) + off, 0, bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fat::cuda_failure("paged_decode_noalloc: clearing tickets", e);
   return fat::launch_paged_decode(a);
 }

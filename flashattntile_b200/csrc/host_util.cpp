@@ -1,5 +1,6 @@
 #include "host_util.h"
 
+#include <atomic>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -31,6 +32,27 @@ EncodeFn resolve_encode() {
 }
 }  // namespace
 
+namespace {
+std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
+std::atomic<int> g_expire_requests{0};
+}  // namespace
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
+uint64_t set_wait_limit_ns(uint64_t ns) {
+  return g_wait_limit_ns.exchange(ns == 0 ? kDefaultWaitLimitNs : ns, std::memory_order_relaxed);
+}
+
+bool take_expire_request() {
+  int n = g_expire_requests.load(std::memory_order_relaxed);
+  while (n > 0) {
+    if (g_expire_requests.compare_exchange_weak(n, n - 1, std::memory_order_relaxed)) return true;
+  }
+  return false;
+}
+
+void request_expiry(int n) { g_expire_requests.store(n > 0 ? n : 0, std::memory_order_relaxed); }
+
 void set_last_error(const std::string& msg) { g_last_error = msg; }
 const char* last_error() { return g_last_error.c_str(); }
 
@@ -50,8 +72,8 @@ int cuda_failure(const char* what, cudaError_t err) {
 }
 
 int current_device() {
-  int dev = 0;
-  cudaGetDevice(&dev);
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   return dev;
 }
 

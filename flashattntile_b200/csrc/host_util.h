@@ -22,7 +22,18 @@ int cuda_failure(const char* what, cudaError_t err);
 
 // Streaming-multiprocessor count of `device` (cached per device).
 int sm_count(int device);
-// Current device of the calling thread.
+// Limit of every bounded in-kernel wait for launches made from now on
+// (fat_set_wait_limit_ns; kDefaultWaitLimitNs until set).
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+uint64_t wait_limit_ns();
+uint64_t set_wait_limit_ns(uint64_t ns);  // returns the previous limit; 0 restores the default
+// Failure-path tests: true for each of the next `n` decode / prefill launches
+// that asked (fat_expire_next_waits), false afterwards.
+bool take_expire_request();
+void request_expiry(int n);
+
+// The calling thread's current CUDA device, or -1 when there is none (no
+// device, or the runtime failed to report it).
 int current_device();
 
 // Raise `func`'s dynamic shared-memory limit to `bytes` once per (kernel, device).

@@ -63,7 +63,10 @@ struct Params {
   long long pt_sb;
   int max_pages, num_pages, page_size;
   int rows_per_box;      // min(page_size, BN): token rows one TMA box brings from one page
+  int cap_tokens;        // min(max_pages * page_size, 2^30): cached lengths are cut to this
   const int* seq_lens_k;
+  unsigned long long wait_ns;  // limit of every bounded wait
+  int expire;            // the MMA issuer first waits on a barrier phase nothing completes (failure-path tests)
 };
 
 // head_dim <= 128: two 128-row query tiles per CTA in ping-pong (S0, S1, O0,
@@ -89,7 +92,9 @@ struct Layout {
   static constexpr int kTile = BM * D * 2;  // one Q, K or V tile
   static constexpr int kStagesK = D <= 64 ? 4 : (D <= 128 ? 3 : 1);
   static constexpr int kStagesV = D <= 64 ? 4 : (D <= 128 ? 2 : 1);
-  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 2 * kTiles + 2) + 16;
+  // q_full, K and V full/empty rings, s_full and p_full per tile, drain, vtail,
+  // never; then the tensor-memory slot and the abort flag.
+  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 3) + 16;
   static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
   static_assert(kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
   static constexpr uint32_t kColS = 0;               // S_t at column kColS + 128 t
@@ -141,7 +146,11 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
   const int q0 = __ldg(p.cu_q + b), q_len = __ldg(p.cu_q + b + 1) - q0;
   const int k0 = kPaged ? 0 : __ldg(p.cu_k + b);
-  const int kv_len = kPaged ? __ldg(p.seq_lens_k + b) : __ldg(p.cu_k + b + 1) - k0;
+  // Paged: a length past the page table is cut to its capacity (and reported),
+  // so tile positions stay in 32 bits and inside the table.
+  const int raw_kv = kPaged ? __ldg(p.seq_lens_k + b) : 0;
+  const int kv_len = kPaged ? min(raw_kv, p.cap_tokens) : __ldg(p.cu_k + b + 1) - k0;
+  if (kPaged && raw_kv > p.cap_tokens && threadIdx.x == 0) raise_error(p.err, FAT_DEVERR_BAD_LENGTH);
   const int m0 = pair * kRowsPerCta;
   if (m0 >= q_len) return;  // uniform for the CTA, before any barrier or allocation
   const int kvh = h / p.group;
@@ -167,8 +176,9 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   const uint32_t p_full = s_full + 8 * kTiles;  // [kTiles]: P_t(j) written, O_t rescaled
   const uint32_t drain = p_full + 8 * kTiles;   // every MMA of the CTA complete
   const uint32_t vtail = drain + 8;             // paged: a partly valid V tile landed (before zeroing its tail)
+  const uint32_t never = vtail + 8;             // initialised, never arrived on (failure-path tests)
   volatile uint32_t* tmem_slot =
-      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 2);
+      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -192,6 +202,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(vtail, 1);
+    mbar_init(never, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -215,13 +226,13 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
           tma_load_3d(sQ + t * L::kTile + cb * BM * 128, &tm_q, q_full, cb * 64, h, q0 + m0 + t * BM);
       for (int j = 0; j < n_max; ++j) {
         const int sk = j % SK, sv = j % SV;
-        if (!mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag)) break;
+        if (!mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag, p.wait_ns)) break;
         mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
 #pragma unroll
         for (int cb = 0; cb < L::kCB; ++cb)
           tma_load_3d(sK + sk * L::kTile + cb * BN * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, k0 + j * BN);
         ++issued_k;
-        if (!mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag)) break;
+        if (!mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag, p.wait_ns)) break;
         mbar_arrive_expect_tx(v_full + 8 * sv, L::kTile);
 #pragma unroll
         for (int cb = 0; cb < L::kCB; ++cb)
@@ -230,11 +241,11 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       }
       if (*abort_flag) {
         // Drain this CTA's own copies before the shared memory goes away.
-        mbar_wait_bounded(q_full, 0, nullptr, nullptr);
+        mbar_wait_bounded(q_full, 0, nullptr, nullptr, p.wait_ns);
         for (int j = max(0, issued_k - SK); j < issued_k; ++j)
-          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr);
+          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr, p.wait_ns);
         for (int j = max(0, issued_v - SV); j < issued_v; ++j)
-          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
+          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr, p.wait_ns);
       }
     } else if (kPaged && warp == kProducerWarp && n_max > 0) {
       // ======================= TMA producer (paged K/V) ========================
@@ -278,7 +289,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         // zeroed in V so that p = 0 there contributes exactly nothing.
         const bool tail = valid_rows < BN || __popc(loaded) * rpb < BN;
         // K tile j.
-        if (lane == 0) ok = mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag);
+        if (lane == 0) ok = mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         if (lane == 0) mbar_arrive_expect_tx(k_full + 8 * sk, bytes);
@@ -288,7 +299,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
                       page);
         ++issued_k;
         // V tile j.
-        if (lane == 0) ok = mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag);
+        if (lane == 0) ok = mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         const uint32_t vbar = tail ? vtail : v_full + 8 * sv;
@@ -299,7 +310,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         ++issued_v;
         if (tail) {
           ++tails;
-          if (lane == 0) ok = mbar_wait_bounded(vtail, (tails - 1) & 1, p.err, abort_flag);
+          if (lane == 0) ok = mbar_wait_bounded(vtail, (tails - 1) & 1, p.err, abort_flag, p.wait_ns);
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
           // Zero every row no copy filled or that lies past the sequence end
@@ -320,12 +331,12 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         }
       }
       if (*abort_flag && lane == 0) {
-        mbar_wait_bounded(q_full, 0, nullptr, nullptr);
+        mbar_wait_bounded(q_full, 0, nullptr, nullptr, p.wait_ns);
         for (int j = max(0, issued_k - SK); j < issued_k; ++j)
-          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr);
+          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr, p.wait_ns);
         for (int j = max(0, issued_v - SV); j < issued_v; ++j)
-          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr);
-        if (tails > 0) mbar_wait_bounded(vtail, (tails - 1) & 1, nullptr, nullptr);
+          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr, p.wait_ns);
+        if (tails > 0) mbar_wait_bounded(vtail, (tails - 1) & 1, nullptr, nullptr, p.wait_ns);
       }
     } else if (warp == kMmaWarp && lane == 0 && n_max > 0) {
       // ============================ MMA issuer ============================
@@ -355,16 +366,19 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
                      kk > 0 ? 1u : acc0);
       };
       int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0;
-      bool ok = mbar_wait_bounded(q_full, 0, p.err, abort_flag);
+      // Failure-path test: a wait that nothing ends runs out after p.wait_ns and
+      // raises the abort flag; the other roles stop at their next wait.
+      if (p.expire) mbar_wait_bounded(never, 0, p.err, abort_flag, p.wait_ns);
+      bool ok = mbar_wait_bounded(q_full, 0, p.err, abort_flag, p.wait_ns);
       for (int j = 0; ok && j <= n_max; ++j) {
-        if (j < n_max && !mbar_wait_bounded(k_full + 8 * sk, kph, p.err, abort_flag)) break;
+        if (j < n_max && !mbar_wait_bounded(k_full + 8 * sk, kph, p.err, abort_flag, p.wait_ns)) break;
         const uint32_t loK = loK0 + uint32_t(sk) * kTileDesc;
         const uint32_t loV = loV0 + uint32_t(sv) * kTileDesc;
         bool v_ready = false;
         // ---- tile 0: O0 += P0 V_{j-1}, then S0 = Q0 K_j^T ----
         if (j >= 1 && j <= n0) {
-          if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag) ||
-              !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag))
+          if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag, p.wait_ns) ||
+              !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag, p.wait_ns))
             break;
           pph0 ^= 1;
           v_ready = true;
@@ -380,8 +394,8 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         if (j <= n0 && (j < n0 || j > 0)) tc::commit(s_full);
         // ---- tile 1 ----
         if (j >= 1 && j <= n1) {
-          if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag) ||
-              (!v_ready && !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag)))
+          if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag, p.wait_ns) ||
+              (!v_ready && !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag, p.wait_ns)))
             break;
           pph1 ^= 1;
           tc::fence_after_sync();
@@ -410,7 +424,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       }
       // Every MMA this thread issued has finished once `drain` completes.
       tc::commit(drain);
-      mbar_wait_bounded(drain, 0, nullptr, nullptr);
+      mbar_wait_bounded(drain, 0, nullptr, nullptr, p.wait_ns);
     }
   } else {
     if constexpr (L::kSplitRegs) regs_inc<L::kRegsSoftmax>();
@@ -427,7 +441,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     float m_used = -CUDART_INF_F, l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < n_t; ++j) {
-      if (!mbar_wait_bounded(sbar, j & 1, p.err, abort_flag)) {
+      if (!mbar_wait_bounded(sbar, j & 1, p.err, abort_flag, p.wait_ns)) {
         ok = false;
         break;
       }
@@ -510,7 +524,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       mbar_arrive(pbar);
     }
     // ---- epilogue: O / l -> global, once the last P.V of this tile completed ----
-    const bool fin = ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag);
+    const bool fin = ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag, p.wait_ns);
     // A warp whose 32 rows all belong to the sequence stages them, 16-bit and
     // 128-byte swizzled, in its rows of the tile's Q buffer (unused once the
     // tile's last MMA completed) and stores them with one TMA copy per 64
@@ -671,6 +685,8 @@ int launch_t(const PrefillArgs& a) {
   p.causal = a.causal ? 1 : 0;
   p.out_f32 = a.out_dtype == FAT_DTYPE_F32;
   p.err = a.error_word;
+  p.wait_ns = wait_limit_ns();
+  p.expire = take_expire_request() ? 1 : 0;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
@@ -727,7 +743,10 @@ int launch_paged_t(const PrefillArgs& a) {
   p.num_pages = int(a.num_pages);
   p.page_size = a.page_size;
   p.rows_per_box = rpb;
+  p.cap_tokens = int(std::min<long long>((long long)a.max_pages * a.page_size, 1ll << 30));
   p.seq_lens_k = a.seq_lens_k;
+  p.wait_ns = wait_limit_ns();
+  p.expire = take_expire_request() ? 1 : 0;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);

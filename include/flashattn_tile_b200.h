@@ -48,8 +48,10 @@ enum {
 
 /* Bits OR-ed into the device error word. */
 enum {
-  FAT_DEVERR_TIMEOUT = 1,  /* a bounded pipeline wait gave up; the output is invalid  */
-  FAT_DEVERR_BAD_PAGE = 2  /* a page id used by a sequence is outside [0, num_pages) */
+  FAT_DEVERR_TIMEOUT = 1,    /* a bounded pipeline wait gave up; the output is invalid  */
+  FAT_DEVERR_BAD_PAGE = 2,   /* a page id used by a sequence is outside [0, num_pages) */
+  FAT_DEVERR_BAD_LENGTH = 4  /* a sequence length exceeds the page table's capacity
+                                (max_pages * page_size); it was cut to that capacity   */
 };
 
 /* Element types. */
@@ -66,6 +68,21 @@ const char* fat_version(void);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* fat_last_error(void);
+
+/* Time limit of every bounded wait inside the decode and prefill kernels,
+ * for launches made after this call, from any thread (default 2 s; 0 restores
+ * it).  A wait that runs out sets FAT_DEVERR_TIMEOUT; the kernel then drains
+ * its own copies and tensor-core work and returns.  Returns the previous limit.
+ * No reference counterpart: the reference's Triton and CUDA kernels have no
+ * in-kernel waits. */
+uint64_t fat_set_wait_limit_ns(uint64_t limit_ns);
+
+/* Failure-path testing: each of the next `launches` decode or prefill kernel
+ * launches (from any thread) first waits on a barrier phase that nothing
+ * completes, so that this wait runs out after the wait limit and the launch
+ * ends with FAT_DEVERR_TIMEOUT (no fault, no hang).  0 cancels requests not
+ * yet taken.  No reference counterpart. */
+void fat_expire_next_waits(int launches);
 
 /*
  * Bytes of scratch fat_paged_decode needs for this problem on `device`.
