@@ -20,6 +20,7 @@ tag and returns the output in that encoding, or fp32 with ``out_f32=True``.
 
 from __future__ import annotations
 
+import contextlib
 import math
 import os
 from concurrent.futures import ThreadPoolExecutor
@@ -43,27 +44,54 @@ def _as_int_list(cu, name):
     return values
 
 
-def attend(qf, kf, vf, causal, scale):
-    """One sequence: ``qf [q_len, H, D]``, ``kf/vf [kv_len, Hkv, D]`` fp32 -> fp32."""
+@contextlib.contextmanager
+def blas_single_thread():
+    """Pin the BLAS / OpenMP pools to one thread while a thread pool of ours runs
+    (``threads`` workers each calling a multi-threaded BLAS oversubscribe the
+    cores several times over).  No-op when threadpoolctl is absent."""
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover - threadpoolctl ships with this image
+        yield
+        return
+    with threadpool_limits(limits=1):
+        yield
+
+
+def _split_heads(qf, kf, vf):
     q_len, heads, dim = qf.shape
-    kv_len, kv_heads, _ = kf.shape
+    kv_heads = kf.shape[1]
     group = heads // kv_heads
     qh = qf.reshape(q_len, kv_heads, group, dim).transpose(1, 2, 0, 3)  # [Hkv, G, q, D]
     kh = np.ascontiguousarray(kf.transpose(1, 2, 0))[:, None]  # [Hkv, 1, D, kv]
     vh = np.ascontiguousarray(vf.transpose(1, 0, 2))[:, None]  # [Hkv, 1, kv, D]
-    out = np.empty((kv_heads, group, q_len, dim), dtype=np.float32)
+    return qh, kh, vh
+
+
+def _attend_rows(qh, kh, vh, r0, r1, offset, causal, scale):
+    """Rows ``[r0, r1)`` of one sequence -> ``[Hkv, G, rows, D]`` fp32 (reference.py:126-140)."""
+    kv_len = kh.shape[-1]
+    s = np.matmul(qh[:, :, r0:r1], kh) * np.float32(scale)  # [Hkv, G, rows, kv]
+    if causal:
+        qi = np.arange(r0, r1)[:, None] + offset
+        kj = np.arange(kv_len)[None, :]
+        s = np.where(kj <= qi, s, np.float32(-np.inf))
+    m = s.max(axis=-1, keepdims=True)
+    e = np.exp(s - m)
+    p = e / e.sum(axis=-1, keepdims=True)
+    return np.matmul(p, vh)
+
+
+def attend(qf, kf, vf, causal, scale):
+    """One sequence: ``qf [q_len, H, D]``, ``kf/vf [kv_len, Hkv, D]`` fp32 -> fp32."""
+    q_len, heads, dim = qf.shape
+    kv_len, kv_heads, _ = kf.shape
+    qh, kh, vh = _split_heads(qf, kf, vf)
+    out = np.empty((kv_heads, heads // kv_heads, q_len, dim), dtype=np.float32)
     offset = kv_len - q_len
     for r0 in range(0, q_len, _ROW_CHUNK):
         r1 = min(q_len, r0 + _ROW_CHUNK)
-        s = np.matmul(qh[:, :, r0:r1], kh) * np.float32(scale)  # [Hkv, G, rows, kv]
-        if causal:
-            qi = np.arange(r0, r1)[:, None] + offset
-            kj = np.arange(kv_len)[None, :]
-            s = np.where(kj <= qi, s, np.float32(-np.inf))
-        m = s.max(axis=-1, keepdims=True)
-        e = np.exp(s - m)
-        p = e / e.sum(axis=-1, keepdims=True)
-        out[:, :, r0:r1] = np.matmul(p, vh)
+        out[:, :, r0:r1] = _attend_rows(qh, kh, vh, r0, r1, offset, causal, scale)
     return out.transpose(2, 0, 1, 3).reshape(q_len, heads, dim)
 
 
@@ -76,8 +104,13 @@ def _check_qkv(q, k, v):
         raise ValueError(f"num_heads ({q.shape[1]}) must be divisible by num_kv_heads ({k.shape[1]})")
 
 
-def attention_varlen(q, k, v, cu_q, cu_k, causal=True, scale=None, dtype="f32", out_f32=False):
-    """``ref_attention_varlen`` (``reference.py:50-142``) on storage arrays."""
+def attention_varlen(q, k, v, cu_q, cu_k, causal=True, scale=None, dtype="f32", out_f32=False, threads=1):
+    """``ref_attention_varlen`` (``reference.py:50-142``) on storage arrays.
+
+    ``threads > 1`` computes the (sequence, row chunk) blocks on a thread pool
+    with BLAS pinned to one thread per worker; every block's arithmetic is the
+    one of the serial loop, so the result is bitwise the same.
+    """
     _check_qkv(q, k, v)
     cq = _as_int_list(cu_q, "cu_seqlens_q")
     ck = _as_int_list(cu_k, "cu_seqlens_k")
@@ -92,6 +125,7 @@ def attention_varlen(q, k, v, cu_q, cu_k, causal=True, scale=None, dtype="f32", 
     kf = numerics.to_f32(k, dtype)
     vf = numerics.to_f32(v, dtype)
     out = np.zeros(q.shape, dtype=np.float32)
+    blocks = []
     for b in range(len(cq) - 1):
         q0, q1, k0, k1 = cq[b], cq[b + 1], ck[b], ck[b + 1]
         q_len, kv_len = q1 - q0, k1 - k0
@@ -103,7 +137,23 @@ def attention_varlen(q, k, v, cu_q, cu_k, causal=True, scale=None, dtype="f32", 
             raise ValueError(
                 f"causal bottom-right alignment requires kv_len >= q_len (sequence {b}: {kv_len} < {q_len})"
             )
-        out[q0:q1] = attend(qf[q0:q1], kf[k0:k1], vf[k0:k1], causal, scale)
+        if threads <= 1:
+            out[q0:q1] = attend(qf[q0:q1], kf[k0:k1], vf[k0:k1], causal, scale)
+            continue
+        split = _split_heads(qf[q0:q1], kf[k0:k1], vf[k0:k1])
+        blocks += [(q0, split, r0, min(q_len, r0 + _ROW_CHUNK), kv_len - q_len)
+                   for r0 in range(0, q_len, _ROW_CHUNK)]
+
+    def one(block):
+        q0, (qh, kh, vh), r0, r1, offset = block
+        rows = _attend_rows(qh, kh, vh, r0, r1, offset, causal, scale)  # [Hkv, G, rows, D]
+        out[q0 + r0:q0 + r1] = rows.transpose(2, 0, 1, 3).reshape(r1 - r0, -1, rows.shape[-1])
+
+    if blocks:
+        # Largest blocks first so the pool finishes together.
+        blocks.sort(key=lambda blk: -(blk[1][1].shape[-1] * (blk[3] - blk[2])))
+        with blas_single_thread(), ThreadPoolExecutor(max_workers=threads) as pool:
+            list(pool.map(one, blocks))
     return out if out_f32 else numerics.from_f32(out, dtype)
 
 
@@ -139,7 +189,7 @@ def attention_paged(q, k_cache, v_cache, page_table, seq_lens, page_size, scale=
                         True, scale)[0]
 
     if threads > 1:
-        with ThreadPoolExecutor(max_workers=threads) as pool:
+        with blas_single_thread(), ThreadPoolExecutor(max_workers=threads) as pool:
             list(pool.map(one, range(batch)))
     else:
         for b in range(batch):
@@ -212,6 +262,7 @@ __all__ = [
     "attention_varlen",
     "attention_paged",
     "attention_dense",
+    "blas_single_thread",
     "decode_split_partials",
     "lse_merge",
     "gather_paged",

@@ -41,3 +41,18 @@ def bytes_attention(mode, batch, q_len, kv_len, num_heads, num_kv_heads, head_di
         kv_bytes = batch * kv_len * num_kv_heads * head_dim * 2 * elem_bytes
         return int(2 * q_bytes + kv_bytes)
     raise ValueError(f"unknown mode {mode!r}")
+
+
+def bytes_decode_paged(seq_lens, num_heads, num_kv_heads, head_dim, page_size, q_bytes=2, kv_bytes=2,
+                       scale_bytes=0) -> int:
+    """Decode bytes of a ragged batch: Q + O, the K/V rows of every cached token,
+    and for 8-bit caches two fp32 scales per used (page, KV head) -- the decode
+    count of ``autotune.py:76-106`` summed per sequence, with the per-token scale
+    accounting of ``quant.py:194-208``."""
+    import math
+
+    lens = [int(x) for x in seq_lens]
+    qo = 2 * len(lens) * num_heads * head_dim * q_bytes
+    kv = sum(lens) * num_kv_heads * head_dim * 2 * kv_bytes
+    scales = sum(math.ceil(n / page_size) for n in lens) * num_kv_heads * 2 * scale_bytes
+    return int(qo + kv + scales)

@@ -210,3 +210,16 @@ def test_bytes_attention_modes():
 def test_cfg2_algorithmic_bytes():
     """The headline roofline numerator: Q + O + K/V rows of every cached token."""
     assert at.bytes_decode_paged([4096] * 32, 32, 8, 128, 16, q_bytes=2, kv_bytes=2) == 537_395_200
+
+
+def test_oracle_and_library_accounting_agree():
+    """bench.py's reference arm counts bytes with the oracle copy (it must not load the library)."""
+    from oracle import work
+
+    assert work.bytes_decode_paged([4096] * 32, 32, 8, 128, 16) == 537_395_200
+    for lens, ps, kvb, sb in (([1, 17, 4095], 16, 2, 0), ([1024, 16384, 7], 32, 1, 4), ([131072] * 8, 64, 2, 0)):
+        assert work.bytes_decode_paged(lens, 64, 8, 128, ps, 2, kvb, sb) == \
+            at.bytes_decode_paged(lens, 64, 8, 128, ps, q_bytes=2, kv_bytes=kvb, scale_bytes=sb)
+    assert work.flops_attention_varlen(32, 128, [512, 1024, 2048, 4096], [512, 1024, 2048, 4096], causal=True) \
+        == at.flops_attention_varlen(32, 128, [512, 1024, 2048, 4096], [512, 1024, 2048, 4096], causal=True) \
+        == 182_599_024_640

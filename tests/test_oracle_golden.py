@@ -56,6 +56,17 @@ def test_prefill_cases_match_reference(name):
     _assert_within_one_ulp(out, c["out"], dt)
     out32 = attention.attention_varlen(*args, dtype=dt, out_f32=True)
     np.testing.assert_allclose(out32, c["out_f32"], atol=F32_ATOL, rtol=F32_RTOL)
+    # The thread-pool mode (the timed CPU baseline) is the same arithmetic.
+    np.testing.assert_array_equal(attention.attention_varlen(*args, dtype=dt, out_f32=True, threads=3), out32)
+
+
+@pytest.mark.parametrize("name", golden_names("decode_"))
+def test_threaded_paged_oracle_is_bitwise_serial(name):
+    c = load_golden(name)
+    args = (c["q"], c["k_cache"], c["v_cache"], c["page_table"], c["seq_lens"], c["meta"]["page_size"])
+    serial = attention.attention_paged(*args, dtype=c["meta"]["dtype"], out_f32=True)
+    np.testing.assert_array_equal(attention.attention_paged(*args, dtype=c["meta"]["dtype"], out_f32=True,
+                                                            threads=3), serial)
 
 
 @pytest.mark.parametrize("mode", ["int8", "float8_e4m3fn"])
