@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
     "fat_last_error": (ctypes.c_char_p, []),
     "fat_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "fat_expire_next_waits": (None, [_i32]),
+    "fat_set_prefill_p_split": (_i32, [_i32]),
     "fat_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "fat_paged_decode": (
         _i32,

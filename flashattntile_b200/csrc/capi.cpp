@@ -21,6 +21,15 @@ uint64_t fat_set_wait_limit_ns(uint64_t limit_ns) { return fat::set_wait_limit_n
 
 void fat_expire_next_waits(int launches) { fat::request_expiry(launches); }
 
+int fat_set_prefill_p_split(int mode) {
+  if (mode < -1 || mode > 2) {
+    fat::set_last_error("prefill p_split must be -1, 0, 1 or 2, got " + std::to_string(mode));
+    return -2;
+  }
+  fat::set_last_error("");
+  return fat::set_prefill_p_split(mode);
+}
+
 size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int num_kv_heads, int head_dim) {
   return fat::decode_workspace_bytes(device, batch, num_heads, num_kv_heads, head_dim);
 }

@@ -35,7 +35,15 @@ EncodeFn resolve_encode() {
 namespace {
 std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
 std::atomic<int> g_expire_requests{0};
+std::atomic<int> g_p_split{-1};
 }  // namespace
+
+int set_prefill_p_split(int mode) { return g_p_split.exchange(mode, std::memory_order_relaxed); }
+
+int prefill_p_split(bool bf16) {
+  const int mode = g_p_split.load(std::memory_order_relaxed);
+  return mode >= 0 ? mode : (bf16 ? 1 : 0);
+}
 
 uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 

@@ -32,6 +32,13 @@ uint64_t set_wait_limit_ns(uint64_t ns);  // returns the previous limit; 0 resto
 bool take_expire_request();
 void request_expiry(int n);
 
+// How prefill feeds P into P.V (fat_set_prefill_p_split): -1 automatic (bf16:
+// a 16-bit remainder on each query tile's first key tile; fp16: rounded), 0
+// rounded once (the reference kernel's arithmetic), 1 remainder on each query
+// tile's first key tile, 2 remainder on every key tile.
+int set_prefill_p_split(int mode);  // returns the previous setting
+int prefill_p_split(bool bf16);     // the mode a launch of that dtype uses
+
 // The calling thread's current CUDA device, or -1 when there is none (no
 // device, or the runtime failed to report it).
 int current_device();

@@ -4,7 +4,10 @@
 // per (query tile, query head, sequence) an online-softmax pass over 128-row
 // K/V tiles with bottom-right causal alignment (query i sees keys
 // j <= i + kv_len - q_len), GQA head h reading KV head h / G, P rounded to the
-// input dtype before P.V (prefill.py:128) and fp32 accumulation.
+// input dtype before P.V (prefill.py:128) and fp32 accumulation.  Optionally
+// (p_split) a key tile's P enters P.V as a 16-bit head plus a 16-bit remainder,
+// keeping the probabilities to ~2^-16: the default for bf16 on each query
+// tile's first key tile, where a row with few keys has all its weight.
 //
 // One CTA per pair of 128-row query tiles (256 rows), warp-specialised:
 //   warps 0-3   softmax of query tile 0, warps 4-7 softmax of query tile 1:
@@ -32,6 +35,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -67,7 +71,13 @@ struct Params {
   const int* seq_lens_k;
   unsigned long long wait_ns;  // limit of every bounded wait
   int expire;            // the MMA issuer first waits on a barrier phase nothing completes (failure-path tests)
+  int p_split;           // P into P.V as head + remainder: 0 never, 1 on each query tile's first key tile, 2 always
 };
+
+// Key tile j of a query tile enters P.V as a 16-bit head plus a 16-bit
+// remainder (two MMA passes, P kept to ~2^-16 relative) instead of P rounded
+// once.  Uniform per CTA: the softmax warps and the MMA issuer decide alike.
+__device__ __forceinline__ bool split_tile(int mode, int j) { return mode == 2 || (mode == 1 && j == 0); }
 
 // head_dim <= 128: two 128-row query tiles per CTA in ping-pong (S0, S1, O0,
 // O1 fill the 512 tensor-memory columns).  head_dim 256: one tile per CTA (S in
@@ -365,6 +375,12 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
           tc::mma_ts(d_tmem, a_tmem + kk * 8, desc(loV + uint32_t((kk * 16 * 128) >> 4), hiV), kIdescPV,
                      kk > 0 ? 1u : acc0);
       };
+      // P.V of key tile jj: the head in columns [0, 64) of the tile's S area,
+      // and for a split tile the remainder in columns [64, 128) accumulated on top.
+      auto issue_p = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t loV, int jj) {
+        issue_pv(d_tmem, a_tmem, loV, jj > 0 ? 1u : 0u);
+        if (split_tile(p.p_split, jj)) issue_pv(d_tmem, a_tmem + BN / 2, loV, 1u);
+      };
       int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0;
       // Failure-path test: a wait that nothing ends runs out after p.wait_ns and
       // raises the abort flag; the other roles stop at their next wait.
@@ -383,7 +399,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
           pph0 ^= 1;
           v_ready = true;
           tc::fence_after_sync();
-          issue_pv(tmem + L::kColO, tmem + L::kColS, loV, j > 1 ? 1u : 0u);
+          issue_p(tmem + L::kColO, tmem + L::kColS, loV, j - 1);
         }
         if (j < n0) {
           tc::fence_after_sync();
@@ -399,7 +415,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
             break;
           pph1 ^= 1;
           tc::fence_after_sync();
-          issue_pv(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j > 1 ? 1u : 0u);
+          issue_p(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j - 1);
         }
         if (j < n1) {
           tc::fence_after_sync();
@@ -499,24 +515,50 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       }
       const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
       float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+      if (!split_tile(p.p_split, j)) {
+        // P rounded to the input dtype (prefill.py:128), packed over S's first 64 columns.
 #pragma unroll
-      for (int c = 0; c < BN / 64; ++c) {
-        uint32_t packed[32];
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t packed[32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float x0, x1, x2, x3;
-          fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
-          fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
-          const float p0 = fast_exp2(x0);
-          const float p1 = fast_exp2(x1);
-          const float p2 = fast_exp2(x2);
-          const float p3 = fast_exp2(x3);
-          add2(sum0, sum1, p0, p1);
-          add2(sum2, sum3, p2, p3);
-          packed[i] = pack2<T>(p0, p1);
-          packed[i + 1] = pack2<T>(p2, p3);
+          for (int i = 0; i < 32; i += 2) {
+            float x0, x1, x2, x3;
+            fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
+            fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
+            const float p0 = fast_exp2(x0);
+            const float p1 = fast_exp2(x1);
+            const float p2 = fast_exp2(x2);
+            const float p3 = fast_exp2(x3);
+            add2(sum0, sum1, p0, p1);
+            add2(sum2, sum3, p2, p3);
+            packed[i] = pack2<T>(p0, p1);
+            packed[i + 1] = pack2<T>(p2, p3);
+          }
+          tc::st32(lane_base + colS + 32 * c, packed);
         }
-        tc::st32(lane_base + colS + 32 * c, packed);
+      } else {
+        // Head in columns [0, 64), remainder p - head in [64, 128): every score
+        // of this S row is already in registers, so those columns are free.
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            float x0, x1, x2, x3;
+            fma2(x0, x1, s[32 * c + 2 * i], s[32 * c + 2 * i + 1], p.scale_log2, -msub);
+            fma2(x2, x3, s[32 * c + 2 * i + 2], s[32 * c + 2 * i + 3], p.scale_log2, -msub);
+            const float p0 = fast_exp2(x0);
+            const float p1 = fast_exp2(x1);
+            const float p2 = fast_exp2(x2);
+            const float p3 = fast_exp2(x3);
+            add2(sum0, sum1, p0, p1);
+            add2(sum2, sum3, p2, p3);
+            split_hi_lo<T>(p0, p1, hi[i], lo[i]);
+            split_hi_lo<T>(p2, p3, hi[i + 1], lo[i + 1]);
+          }
+          tc::st16(lane_base + colS + 16 * c, hi);
+          tc::st16(lane_base + colS + BN / 2 + 16 * c, lo);
+        }
       }
       l_sum += (sum0 + sum1) + (sum2 + sum3);
       tc::wait_st();
@@ -687,6 +729,7 @@ int launch_t(const PrefillArgs& a) {
   p.err = a.error_word;
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
+  p.p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
@@ -747,6 +790,7 @@ int launch_paged_t(const PrefillArgs& a) {
   p.seq_lens_k = a.seq_lens_k;
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
+  p.p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);

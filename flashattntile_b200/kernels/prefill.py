@@ -12,6 +12,8 @@ validated as in the reference and otherwise ignored.
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from .. import _config, _lib
@@ -19,6 +21,34 @@ from .. import _config, _lib
 DEFAULT_CONFIG = {"BLOCK_M": 64, "BLOCK_N": 64, "num_warps": 4, "num_stages": 3}
 HAS_TRITON = False
 HAS_CUDA_KERNELS = _lib.available()
+
+# How P enters the P.V product (``fat_set_prefill_p_split``).  The reference
+# kernel rounds P to the input dtype once (``prefill.py:128``); for bf16 that
+# alone moves the outputs of rows with few keys by up to ~4e-3, so by default
+# bf16 feeds each query tile's first key tile as a 16-bit head plus a 16-bit
+# remainder (one extra P.V pass per query tile).
+P_SPLIT_MODES = {"auto": -1, "rounded": 0, "first_tile": 1, "all_tiles": 2}
+
+
+def set_p_precision(mode: str) -> str:
+    """Set the P.V precision mode for later prefill launches; returns the previous one.
+
+    ``"auto"`` (default: bf16 ``"first_tile"``, fp16 ``"rounded"``), ``"rounded"``
+    (the reference's arithmetic), ``"first_tile"``, ``"all_tiles"``."""
+    if mode not in P_SPLIT_MODES:
+        raise ValueError(f"unknown P precision mode {mode!r}; expected one of {sorted(P_SPLIT_MODES)}")
+    prev = _lib.load().fat_set_prefill_p_split(P_SPLIT_MODES[mode])
+    return {v: k for k, v in P_SPLIT_MODES.items()}[prev]
+
+
+@contextlib.contextmanager
+def p_precision(mode: str):
+    """Context manager form of :func:`set_p_precision`."""
+    prev = set_p_precision(mode)
+    try:
+        yield
+    finally:
+        set_p_precision(prev)
 
 
 def _resolve_config(config: dict | None) -> dict:

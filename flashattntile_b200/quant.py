@@ -75,7 +75,12 @@ def quantize_kv_pages(k_cache: torch.Tensor, v_cache: torch.Tensor, mode: str = 
 
     def one(x: torch.Tensor):
         xf = x.detach().float()
-        scale = (xf.abs().amax(dim=(1, 3)) / max_val).clamp_min(min_scale)
+        # Divide by a tensor, not a Python number: torch's CUDA kernels turn a
+        # division by a scalar into a multiplication by its reciprocal, which can
+        # differ from the correctly rounded quotient in the last bit.  This way
+        # the scales (and so the codes) are the same on every device.
+        amax = xf.abs().amax(dim=(1, 3))
+        scale = (amax / torch.full_like(amax, max_val)).clamp_min(min_scale)
         y = xf / scale[:, None, :, None]
         if mode == "int8":
             codes = y.round().clamp_(-max_val, max_val).to(dtype)

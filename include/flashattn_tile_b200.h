@@ -84,6 +84,19 @@ uint64_t fat_set_wait_limit_ns(uint64_t limit_ns);
  * yet taken.  No reference counterpart. */
 void fat_expire_next_waits(int launches);
 
+/* How the prefill kernels feed the probabilities P into the P.V product, for
+ * launches made after this call, from any thread.  The reference kernel
+ * rounds P to the input dtype once (kernels/prefill.py:128); with bf16's 8-bit
+ * significand that alone moves outputs of rows with few keys by up to ~4e-3.
+ *   -1  automatic (default): bf16 uses mode 1, fp16 mode 0
+ *    0  P rounded to the input dtype once (the reference's arithmetic)
+ *    1  on each query tile's first key tile, P enters as a 16-bit head plus a
+ *       16-bit remainder (a second P.V pass over that tile; ~2^-16 relative)
+ *    2  head plus remainder on every key tile (twice the P.V work)
+ * Returns the previous setting, or -2 (message in fat_last_error) for a mode
+ * outside [-1, 2].  No reference counterpart. */
+int fat_set_prefill_p_split(int mode);
+
 /*
  * Bytes of scratch fat_paged_decode needs for this problem on `device`.
  * The caller zero-fills the buffer once; every successful call leaves it
