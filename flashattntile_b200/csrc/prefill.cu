@@ -6,8 +6,8 @@
 // j <= i + kv_len - q_len), GQA head h reading KV head h / G, P rounded to the
 // input dtype before P.V (prefill.py:128) and fp32 accumulation.  Optionally
 // (p_split) a key tile's P enters P.V as a 16-bit head plus a 16-bit remainder,
-// keeping the probabilities to ~2^-16: the default for bf16 on each query
-// tile's first key tile, where a row with few keys has all its weight.
+// keeping the probabilities to ~2^-16: for bf16 by default on every key tile
+// that holds a key weighing more than 1/16 of its row's sum so far.
 //
 // One CTA per pair of 128-row query tiles (256 rows), warp-specialised:
 //   warps 0-3   softmax of query tile 0, warps 4-7 softmax of query tile 1:
@@ -71,13 +71,17 @@ struct Params {
   const int* seq_lens_k;
   unsigned long long wait_ns;  // limit of every bounded wait
   int expire;            // the MMA issuer first waits on a barrier phase nothing completes (failure-path tests)
-  int p_split;           // P into P.V as head + remainder: 0 never, 1 on each query tile's first key tile, 2 always
+  int p_split;           // P into P.V as head + remainder: 0 never, 1 where a key weighs (vote), 2 always
 };
 
-// Key tile j of a query tile enters P.V as a 16-bit head plus a 16-bit
-// remainder (two MMA passes, P kept to ~2^-16 relative) instead of P rounded
-// once.  Uniform per CTA: the softmax warps and the MMA issuer decide alike.
-__device__ __forceinline__ bool split_tile(int mode, int j) { return mode == 2 || (mode == 1 && j == 0); }
+// p_split == 1: a key tile of a query tile enters P.V as a 16-bit head plus a
+// 16-bit remainder (a second P.V pass; P kept to ~2^-16 relative) when any of
+// its rows has a key whose probability exceeds kSplitTheta of the row's sum so
+// far.  That sum only grows, so every key of an unsplit tile ends with weight
+// <= kSplitTheta, and the 16-bit rounding of its P moves the output by at most
+// 2^-8 * kSplitTheta * |v|; rows with few keys, or a few dominant keys, are
+// always split.
+constexpr float kSplitTheta = 1.0f / 16.0f;
 
 // head_dim <= 128: two 128-row query tiles per CTA in ping-pong (S0, S1, O0,
 // O1 fill the 512 tensor-memory columns).  head_dim 256: one tile per CTA (S in
@@ -103,8 +107,9 @@ struct Layout {
   static constexpr int kStagesK = D <= 64 ? 4 : (D <= 128 ? 3 : 1);
   static constexpr int kStagesV = D <= 64 ? 4 : (D <= 128 ? 2 : 1);
   // q_full, K and V full/empty rings, s_full and p_full per tile, drain, vtail,
-  // never; then the tensor-memory slot and the abort flag.
-  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 3) + 16;
+  // never; then the tensor-memory slot, the abort flag and the split votes
+  // ([tile][warp][parity] ints).
+  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 3) + 8 + 4 * 8 * kTiles;
   static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
   static_assert(kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
   static constexpr uint32_t kColS = 0;               // S_t at column kColS + 128 t
@@ -190,6 +195,9 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   volatile uint32_t* tmem_slot =
       reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Split votes of the softmax warps, read by the MMA issuer after p_full:
+  // [tile][warp of the warpgroup][key tile parity].
+  volatile int* votes = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (warp == kMmaWarp) {
@@ -375,11 +383,17 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
           tc::mma_ts(d_tmem, a_tmem + kk * 8, desc(loV + uint32_t((kk * 16 * 128) >> 4), hiV), kIdescPV,
                      kk > 0 ? 1u : acc0);
       };
-      // P.V of key tile jj: the head in columns [0, 64) of the tile's S area,
-      // and for a split tile the remainder in columns [64, 128) accumulated on top.
-      auto issue_p = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t loV, int jj) {
+      // P.V of key tile jj of query tile t: the head in columns [0, 64) of the
+      // tile's S area, and for a split tile the remainder in columns [64, 128)
+      // accumulated on top (votes are visible: p_full's arrivals release them).
+      auto issue_p = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t loV, int jj, int t) {
         issue_pv(d_tmem, a_tmem, loV, jj > 0 ? 1u : 0u);
-        if (split_tile(p.p_split, jj)) issue_pv(d_tmem, a_tmem + BN / 2, loV, 1u);
+        bool split = p.p_split == 2;
+        if (p.p_split == 1) {
+          const volatile int* v = votes + t * 8 + (jj & 1);
+          split = (v[0] | v[2] | v[4] | v[6]) != 0;
+        }
+        if (split) issue_pv(d_tmem, a_tmem + BN / 2, loV, 1u);
       };
       int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0;
       // Failure-path test: a wait that nothing ends runs out after p.wait_ns and
@@ -399,7 +413,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
           pph0 ^= 1;
           v_ready = true;
           tc::fence_after_sync();
-          issue_p(tmem + L::kColO, tmem + L::kColS, loV, j - 1);
+          issue_p(tmem + L::kColO, tmem + L::kColS, loV, j - 1, 0);
         }
         if (j < n0) {
           tc::fence_after_sync();
@@ -415,7 +429,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
             break;
           pph1 ^= 1;
           tc::fence_after_sync();
-          issue_p(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j - 1);
+          issue_p(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j - 1, 1);
         }
         if (j < n1) {
           tc::fence_after_sync();
@@ -515,26 +529,39 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       }
       const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
       float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-      if (!split_tile(p.p_split, j)) {
+      // Probabilities in place of the scores.
+#pragma unroll
+      for (int i = 0; i < BN; i += 4) {
+        float x0, x1, x2, x3;
+        fma2(x0, x1, s[i], s[i + 1], p.scale_log2, -msub);
+        fma2(x2, x3, s[i + 2], s[i + 3], p.scale_log2, -msub);
+        s[i] = fast_exp2(x0);
+        s[i + 1] = fast_exp2(x1);
+        s[i + 2] = fast_exp2(x2);
+        s[i + 3] = fast_exp2(x3);
+        add2(sum0, sum1, s[i], s[i + 1]);
+        add2(sum2, sum3, s[i + 2], s[i + 3]);
+      }
+      l_sum += (sum0 + sum1) + (sum2 + sum3);
+      bool split = p.p_split == 2;
+      if (p.p_split == 1) split = __any_sync(0xffffffffu, fast_exp2(mx - msub) > kSplitTheta * l_sum);
+      if (!split) {
         // P rounded to the input dtype (prefill.py:128), packed over S's first 64 columns.
 #pragma unroll
         for (int c = 0; c < BN / 64; ++c) {
           uint32_t packed[32];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float x0, x1, x2, x3;
-            fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
-            fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
-            const float p0 = fast_exp2(x0);
-            const float p1 = fast_exp2(x1);
-            const float p2 = fast_exp2(x2);
-            const float p3 = fast_exp2(x3);
-            add2(sum0, sum1, p0, p1);
-            add2(sum2, sum3, p2, p3);
-            packed[i] = pack2<T>(p0, p1);
-            packed[i + 1] = pack2<T>(p2, p3);
-          }
+          for (int i = 0; i < 32; ++i) packed[i] = pack2<T>(s[64 * c + 2 * i], s[64 * c + 2 * i + 1]);
           tc::st32(lane_base + colS + 32 * c, packed);
+        }
+        if (p.p_split == 1) {
+          // Another warp of this tile may vote to split: the remainder pass then
+          // reads these rows' columns [64, 128), which must hold zeros.
+          uint32_t zero[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) zero[i] = 0u;
+          tc::st32(lane_base + colS + BN / 2, zero);
+          tc::st32(lane_base + colS + BN / 2 + 32, zero);
         }
       } else {
         // Head in columns [0, 64), remainder p - head in [64, 128): every score
@@ -543,24 +570,12 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t hi[16], lo[16];
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            float x0, x1, x2, x3;
-            fma2(x0, x1, s[32 * c + 2 * i], s[32 * c + 2 * i + 1], p.scale_log2, -msub);
-            fma2(x2, x3, s[32 * c + 2 * i + 2], s[32 * c + 2 * i + 3], p.scale_log2, -msub);
-            const float p0 = fast_exp2(x0);
-            const float p1 = fast_exp2(x1);
-            const float p2 = fast_exp2(x2);
-            const float p3 = fast_exp2(x3);
-            add2(sum0, sum1, p0, p1);
-            add2(sum2, sum3, p2, p3);
-            split_hi_lo<T>(p0, p1, hi[i], lo[i]);
-            split_hi_lo<T>(p2, p3, hi[i + 1], lo[i + 1]);
-          }
+          for (int i = 0; i < 16; ++i) split_hi_lo<T>(s[32 * c + 2 * i], s[32 * c + 2 * i + 1], hi[i], lo[i]);
           tc::st16(lane_base + colS + 16 * c, hi);
           tc::st16(lane_base + colS + BN / 2 + 16 * c, lo);
         }
       }
-      l_sum += (sum0 + sum1) + (sum2 + sum3);
+      if (p.p_split == 1 && lane == 0) votes[t * 8 + (warp & 3) * 2 + (j & 1)] = split ? 1 : 0;
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(pbar);

@@ -23,18 +23,20 @@ HAS_TRITON = False
 HAS_CUDA_KERNELS = _lib.available()
 
 # How P enters the P.V product (``fat_set_prefill_p_split``).  The reference
-# kernel rounds P to the input dtype once (``prefill.py:128``); for bf16 that
-# alone moves the outputs of rows with few keys by up to ~4e-3, so by default
-# bf16 feeds each query tile's first key tile as a 16-bit head plus a 16-bit
-# remainder (one extra P.V pass per query tile).
-P_SPLIT_MODES = {"auto": -1, "rounded": 0, "first_tile": 1, "all_tiles": 2}
+# kernel rounds P to the input dtype once (``prefill.py:128``); with bf16 that
+# alone moves outputs by up to ~4e-3 where a row has few keys or a few keys
+# dominate it.  By default bf16 feeds a key tile as a 16-bit head plus a 16-bit
+# remainder (a second P.V pass over that tile) whenever one of its keys holds
+# more than 1/16 of its row's probability sum so far ("adaptive"): every key
+# left rounded then weighs at most 1/16 in the output.
+P_SPLIT_MODES = {"auto": -1, "rounded": 0, "adaptive": 1, "all_tiles": 2}
 
 
 def set_p_precision(mode: str) -> str:
     """Set the P.V precision mode for later prefill launches; returns the previous one.
 
-    ``"auto"`` (default: bf16 ``"first_tile"``, fp16 ``"rounded"``), ``"rounded"``
-    (the reference's arithmetic), ``"first_tile"``, ``"all_tiles"``."""
+    ``"auto"`` (default: bf16 ``"adaptive"``, fp16 ``"rounded"``), ``"rounded"``
+    (the reference's arithmetic), ``"adaptive"``, ``"all_tiles"``."""
     if mode not in P_SPLIT_MODES:
         raise ValueError(f"unknown P precision mode {mode!r}; expected one of {sorted(P_SPLIT_MODES)}")
     prev = _lib.load().fat_set_prefill_p_split(P_SPLIT_MODES[mode])

@@ -90,8 +90,11 @@ void fat_expire_next_waits(int launches);
  * significand that alone moves outputs of rows with few keys by up to ~4e-3.
  *   -1  automatic (default): bf16 uses mode 1, fp16 mode 0
  *    0  P rounded to the input dtype once (the reference's arithmetic)
- *    1  on each query tile's first key tile, P enters as a 16-bit head plus a
- *       16-bit remainder (a second P.V pass over that tile; ~2^-16 relative)
+ *    1  a key tile's P enters as a 16-bit head plus a 16-bit remainder (a
+ *       second P.V pass over that tile; ~2^-16 relative) when one of its keys
+ *       holds more than 1/16 of its row's probability sum so far; every other
+ *       key ends with weight <= 1/16, so its rounding moves an output by at
+ *       most 2^-12 of |v|
  *    2  head plus remainder on every key tile (twice the P.V work)
  * Returns the previous setting, or -2 (message in fat_last_error) for a mode
  * outside [-1, 2].  No reference counterpart. */

@@ -45,6 +45,25 @@ def main() -> None:
         want = oatt.attention_paged(to_np(q), to_np(k), to_np(v), to_np(table), to_np(lens_t), ps, dtype="f16")
         worst = assert_parity_16bit(out, want, torch.float16)
         print(f"rank {rank}: max-abs {worst:.3e} over {math.prod(out.shape)} outputs")
+
+        # Head-first plan: this rank keeps a compact copy of its KV-head slice
+        # (sequence split inside the head group) and decodes with no exchange.
+        from flashattntile_b200 import sharding
+
+        cache = PagedKVCache(k.to(dev), v.to(dev), table.to(dev), lens_t.to(dev), ps)
+        plan = sharding.plan_shards(kvh, world, "sequence")
+        sh = plan.shard(rank, len(lens))
+        mine_cache = sharding.shard_cache(cache, plan, rank, copy=True)
+        h0, h1 = sh.query_heads(heads, kvh)
+        part = sharding.sharded_decode(sharding.shard_query(q.to(dev), plan, rank).contiguous(), mine_cache, plan,
+                                       rank)
+        assert_parity_16bit(part, want[sh.seq0:sh.seq1, h0:h1], torch.float16)
+
+        # Page split over all ranks: partial rows go to their owners (all-to-all), LSE merge.
+        pplan = sharding.plan_shards(kvh, world, "page", head_groups=1)
+        rows = sharding.sharded_decode(q.to(dev), sharding.shard_cache(cache, pplan, rank), pplan, rank)
+        r0, r1 = sharding.owner_rows(len(lens) * heads, world)[rank]
+        assert_parity_16bit(rows, want.reshape(len(lens) * heads, dim)[r0:r1], torch.float16)
         dist.barrier()
         print("sp_worker ok")
     finally:
