@@ -13,10 +13,11 @@ metric = decode HBM GB/s = algorithmic bytes (Q + K + V + O, FlashAttnTile's
   over ranks.
 * ``e2e``: the same step through the public op
   ``torch.ops.flashattn_tile.paged_decode`` as a serving loop calls it: every
-  step's inputs (q, page table, seq_lens) copied in from pinned host memory on
-  a copy stream (double-buffered, so step i+1's upload overlaps step i's
-  kernel), the default host-side validation, and the output copied back to
-  pinned host memory on a second copy stream; the KV cache stays resident.
+  step's inputs (q, page table, seq_lens) packed in one pinned host buffer
+  and uploaded in one copy on a copy stream (two input sets, so uploads run
+  ahead of the kernels), the default host-side validation, and the output
+  copied back to pinned host memory on the same copy stream; the KV cache
+  stays resident.
   Timed on the device from the first upload to the last download.
 * ``cpu_baseline``: the numpy restatement of the reference's fp32 path
   (``oracle/``) on the whole cfg2 batch, timed on this host's cores.
@@ -180,51 +181,49 @@ def roofline(bound: str, work: float, ms: float, peaks: dict, **extra) -> dict:
     return out
 
 
-def e2e_pipelined(device, steps: int, warmup: int, host_in: list, dev_sets: list, run, out_like: torch.Tensor):
+def e2e_pipelined(device, steps: int, warmup: int, host_in: list, dev_sets: list, run, out_like: torch.Tensor,
+                  views: list | None = None):
     """Device ms per step of ``run(inputs) -> output`` with every step's inputs
     uploaded from pinned host memory and its output read back to pinned host
     memory, inside the timed region.
 
-    Uploads run on one copy stream into two alternating device input sets (step
-    i+1's upload overlaps step i's compute; an upload waits until the step that
-    last used its set finished), downloads on another copy stream, compute on
-    the current stream.  The region starts before the first upload and ends
-    after the last download.  Returns (ms per step, last output on the host)."""
+    Two device input sets alternate: once step i's compute has finished, one
+    copy stream reads its output back and uploads step i+2's inputs into the
+    set step i used, so uploads and downloads overlap the next step's compute.
+    The region starts before the first upload and ends after the last
+    download.  ``views`` (per input set): what ``run`` gets instead of the set's
+    buffers (views into one packed buffer: one copy per step).  Returns (ms per
+    step, last output on the host)."""
     comp = torch.cuda.current_stream(device)
-    up = torch.cuda.Stream(device)
-    down = torch.cuda.Stream(device)
+    copy = torch.cuda.Stream(device)
     host_out = [torch.empty(out_like.shape, dtype=out_like.dtype).pin_memory() for _ in range(2)]
 
     def one_pass(n: int) -> float:
         ready = [torch.cuda.Event() for _ in range(n)]
         used = [torch.cuda.Event() for _ in range(n)]
-        outs = []
+        outs = []  # kept until the end of the pass: no output is freed under a pending copy
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(comp)
-        up.wait_event(start)
-
-        def upload(i):
-            with torch.cuda.stream(up):
-                if i >= 2:
-                    up.wait_event(used[i - 2])
-                for h, d in zip(host_in, dev_sets[i % 2]):
+        with torch.cuda.stream(copy):
+            copy.wait_event(start)
+            for i in range(min(2, n)):
+                for h, d in zip(host_in, dev_sets[i]):
                     d.copy_(h, non_blocking=True)
-                ready[i].record(up)
-
-        upload(0)
+                ready[i].record(copy)
         for i in range(n):
-            if i + 1 < n:
-                upload(i + 1)
             comp.wait_event(ready[i])
-            o = run(dev_sets[i % 2])
+            o = run(dev_sets[i % 2] if views is None else views[i % 2])
             used[i].record(comp)
-            with torch.cuda.stream(down):
-                down.wait_event(used[i])
-                host_out[i % 2].copy_(o, non_blocking=True)
-            o.record_stream(down)
             outs.append(o)
+            with torch.cuda.stream(copy):
+                copy.wait_event(used[i])
+                host_out[i % 2].copy_(o, non_blocking=True)
+                if i + 2 < n:
+                    for h, d in zip(host_in, dev_sets[i % 2]):
+                        d.copy_(h, non_blocking=True)
+                    ready[i + 2].record(copy)
         done = torch.cuda.Event()
-        done.record(down)
+        done.record(copy)
         comp.wait_event(done)
         end.record(comp)
         torch.cuda.synchronize()
@@ -237,6 +236,27 @@ def e2e_pipelined(device, steps: int, warmup: int, host_in: list, dev_sets: list
 
 def nbytes_of(tensors) -> int:
     return int(sum(t.numel() * t.element_size() for t in tensors))
+
+
+def packed_inputs(device, tensors):
+    """One pinned host buffer holding ``tensors`` back to back (16-byte aligned
+    pieces) and two device buffers with views of the same layout, so a step's
+    inputs go up in one copy: ``(host [buffer], dev_sets [[buffer]], views per set)``."""
+    import numpy as np
+
+    offs, n = [], 0
+    for t in tensors:
+        offs.append(n)
+        n += (t.numel() * t.element_size() + 15) // 16 * 16
+    host = torch.empty(n, dtype=torch.uint8).pin_memory()
+    for t, o in zip(tensors, offs):
+        b = t.numel() * t.element_size()
+        host[o:o + b].copy_(torch.from_numpy(np.frombuffer(t.detach().cpu().contiguous().numpy().tobytes(),
+                                                           dtype=np.uint8)))
+    dev_bufs = [torch.empty(n, dtype=torch.uint8, device=device) for _ in range(2)]
+    views = [[buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for t, o in zip(tensors, offs)]
+             for buf in dev_bufs]
+    return [host], [[buf] for buf in dev_bufs], views
 
 
 def _cpu_timed(fn, iters: int) -> tuple[float, float]:
@@ -363,8 +383,7 @@ def main() -> None:
     dev_err = _lib.read_device_error(device)
 
     # ---- e2e through the public op with host buffers ----
-    host_in = [q.cpu().pin_memory(), table.cpu().pin_memory(), lens.cpu().pin_memory()]
-    dev_sets = [[torch.empty_like(q), torch.empty_like(table), torch.empty_like(lens)] for _ in range(2)]
+    host_in, dev_sets, views = packed_inputs(device, [q, table, lens])
 
     def e2e_run(d):
         return torch.ops.flashattn_tile.paged_decode(d[0], k, v, d[1], d[2], c["page_size"], scale, 1)
@@ -372,7 +391,7 @@ def main() -> None:
     e2e_steps = max(10, args.steps // 2)
     if dist is not None:
         dist.barrier()
-    e2e_ms, o_h = e2e_pipelined(device, e2e_steps, args.warmup, host_in, dev_sets, e2e_run, q)
+    e2e_ms, o_h = e2e_pipelined(device, e2e_steps, args.warmup, host_in, dev_sets, e2e_run, q, views)
     (e2e_ms,) = max_over_ranks([e2e_ms], device, dist)
     e2e_ok = torch.equal(o_h.to(device), out)
 
@@ -414,8 +433,9 @@ def main() -> None:
             "e2e": {"value": round(world * nbytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": nbytes_of(host_in),
                     "d2h_bytes_per_step": nbytes_of([q]),
-                    "path": "torch.ops.flashattn_tile.paged_decode, default validation; pinned host q/table/lens in "
-                            "(copy stream, double-buffered), output to pinned host (second copy stream)",
+                    "path": "torch.ops.flashattn_tile.paged_decode, default validation; q/table/lens packed in one "
+                            "pinned host buffer, one upload per step (copy stream, two input sets), output to pinned "
+                            "host (same copy stream)",
                     "matches_device_path": bool(e2e_ok)},
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
@@ -801,13 +821,13 @@ def run_quant(device, args, peaks, dist=None, cpu: bool = False) -> dict:
             dist.barrier()
         times = time_steps(step, max(10, args.steps // 2), args.warmup)
         ms, = max_over_ranks([statistics.mean(times)], device, dist)
-        host_in = [q.cpu().pin_memory(), table.cpu().pin_memory(), lens.cpu().pin_memory()]
-        dev_sets = [[torch.empty_like(q), torch.empty_like(table), torch.empty_like(lens)] for _ in range(2)]
+        host_in, dev_sets, views = packed_inputs(device, [q, table, lens])
 
         def e2e_run(d):
             return torch.ops.flashattn_tile.paged_decode_quant(d[0], kq, vq, ks, vs, d[1], d[2], ps, dim ** -0.5, 1)
 
-        e2e_ms, o_h = e2e_pipelined(device, max(10, args.steps // 4), args.warmup, host_in, dev_sets, e2e_run, q)
+        e2e_ms, o_h = e2e_pipelined(device, max(10, args.steps // 4), args.warmup, host_in, dev_sets, e2e_run, q,
+                                    views)
         e2e_ms, = max_over_ranks([e2e_ms], device, dist)
         entry = {"value": round(world * nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms": round(ms, 4),
                  "n_gpus": world, "scaling": "weak", "global_batch": global_batch, "batch_per_gpu": batch,
@@ -816,8 +836,8 @@ def run_quant(device, args, peaks, dist=None, cpu: bool = False) -> dict:
                  "e2e": {"value": round(world * nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                          "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": nbytes_of(host_in),
                          "d2h_bytes_per_step": nbytes_of([q]),
-                         "path": "torch.ops.flashattn_tile.paged_decode_quant, default validation, pinned host "
-                                 "q/table/lens in and output out (copy streams)",
+                         "path": "torch.ops.flashattn_tile.paged_decode_quant, default validation, q/table/lens "
+                                 "packed in one pinned upload per step, output to pinned host (one copy stream)",
                          "matches_device_path": bool(torch.equal(o_h.to(device), out))}}
         if cpu:
             entry["cpu_baseline"] = cpu_quant_sample(q, kq, vq, ks, vs, table, lens, ps, mode, seqs=8, iters=3,
@@ -873,7 +893,7 @@ def run_prefill(device, args, peaks, cpu: bool = False) -> dict:
                         "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": nbytes_of(host_in),
                         "d2h_bytes_per_step": nbytes_of([q3]),
                         "path": "torch.ops.flashattn_tile.prefill_varlen, default validation, pinned host q/k/v/cu "
-                                "in and output out (copy streams); bound by PCIe, not the kernel",
+                                "in and output out (one copy stream); bound by PCIe, not the kernel",
                         "matches_device_path": bool(torch.equal(o_h.to(device), ref))}
         if cpu:
             entry["cpu_baseline"] = cpu_prefill_cfg3(q3, k3, v3, cu, tag, flops, iters=3)

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64,
          _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp],
     ),
+    "fat_paged_decode_call": (_i32, [_vp]),
     "fat_lse_merge": (_i32, [_vp, _i64, _vp, _i64, _i32, _i64, _i32, _vp, _i32, _vp, _vp]),
     "fat_paged_decode_noalloc": (
         _i32,
@@ -91,6 +92,26 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp],
     ),
 }
+
+
+
+class DecodeCall(ctypes.Structure):
+    """``fat_decode_call`` (include/flashattn_tile_b200.h): fat_paged_decode_lse's
+    arguments in one struct, plus the optional value-statistics outputs."""
+
+    _fields_ = [
+        ("q", _vp), ("q_stride_b", _i64), ("q_stride_h", _i64), ("k_cache", _vp), ("v_cache", _vp),
+        ("kv_stride_page", _i64), ("kv_stride_slot", _i64), ("kv_stride_head", _i64), ("num_pages", _i64),
+        ("page_table", _vp), ("page_table_stride", _i64), ("max_pages", _i64), ("seq_lens", _vp),
+        ("k_scale", _vp), ("v_scale", _vp), ("scale_stride_page", _i64), ("out", _vp), ("out_stride_b", _i64),
+        ("out_stride_h", _i64), ("lse", _vp), ("lse_stride_b", _i64), ("batch", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32), ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("page_size", ctypes.c_int32), ("q_dtype", ctypes.c_int32), ("kv_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32), ("softmax_scale", ctypes.c_float), ("split_k_hint", ctypes.c_int32),
+        ("workspace", _vp), ("workspace_bytes", _sz), ("error_word", _vp), ("stream", _vp), ("stats_out", _vp),
+        ("stats_scratch", _vp), ("stats_event", _vp),
+    ]
+
 
 _LOCK = threading.Lock()
 _LIB: ctypes.CDLL | None = None
@@ -203,6 +224,16 @@ def reset_workspace(device: torch.device) -> None:
         _ERR[key].zero_()
 
 
+def stats_buffers(index: int, stream: int, device: torch.device):
+    """This stream's (device scratch, pinned host int32[4], event) for the value statistics."""
+    bufs = _STATS.get((index, stream))
+    if bufs is None:
+        bufs = (torch.zeros(4, dtype=torch.int32, device=device), torch.zeros(4, dtype=torch.int32).pin_memory(),
+                torch.cuda.Event())
+        _STATS[(index, stream)] = bufs
+    return bufs
+
+
 def cache_value_stats_async(seq_lens: torch.Tensor, page_table: torch.Tensor,
                             page_size: int) -> tuple[torch.Tensor, torch.cuda.Event]:
     """Queue ``fat_cache_value_stats`` on the current stream: returns the pinned
@@ -212,11 +243,7 @@ def cache_value_stats_async(seq_lens: torch.Tensor, page_table: torch.Tensor,
     lib = load()
     dev = seq_lens.device
     index, stream = _key(dev)
-    bufs = _STATS.get((index, stream))
-    if bufs is None:
-        bufs = (torch.zeros(4, dtype=torch.int32, device=dev), torch.zeros(4, dtype=torch.int32).pin_memory(),
-                torch.cuda.Event())
-        _STATS[(index, stream)] = bufs
+    bufs = stats_buffers(index, stream, dev)
     if page_table.stride(1) != 1:
         page_table = page_table.contiguous()
     if not seq_lens.is_contiguous():

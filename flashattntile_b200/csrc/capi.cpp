@@ -120,6 +120,28 @@ int fat_paged_decode_lse(const void* q, int64_t q_stride_b, int64_t q_stride_h, 
                       workspace, workspace_bytes, error_word, stream);
 }
 
+int fat_paged_decode_call(const fat_decode_call* c) {
+  fat::set_last_error("");
+  if (c == nullptr) return fat::invalid("paged_decode_call: null argument struct");
+  if (c->stats_out != nullptr) {
+    const int rc = fat::cache_value_stats(c->seq_lens, c->page_table, c->page_table_stride, c->batch, c->max_pages,
+                                          c->page_size, c->stats_scratch, c->stats_out,
+                                          static_cast<cudaStream_t>(c->stream));
+    if (rc != FAT_OK) return rc;
+    if (c->stats_event != nullptr) {
+      const cudaError_t e =
+          cudaEventRecord(static_cast<cudaEvent_t>(c->stats_event), static_cast<cudaStream_t>(c->stream));
+      if (e != cudaSuccess) return fat::cuda_failure("paged_decode_call: recording stats_event", e);
+    }
+  }
+  return decode_entry(c->q, c->q_stride_b, c->q_stride_h, c->k_cache, c->v_cache, c->kv_stride_page,
+                      c->kv_stride_slot, c->kv_stride_head, c->num_pages, c->page_table, c->page_table_stride,
+                      c->max_pages, c->seq_lens, c->k_scale, c->v_scale, c->scale_stride_page, c->out,
+                      c->out_stride_b, c->out_stride_h, c->lse, c->lse_stride_b, c->batch, c->num_heads,
+                      c->num_kv_heads, c->head_dim, c->page_size, c->q_dtype, c->kv_dtype, c->out_dtype,
+                      c->softmax_scale, c->split_k_hint, c->workspace, c->workspace_bytes, c->error_word, c->stream);
+}
+
 int fat_lse_merge(const float* o, int64_t o_part_stride, const float* lse, int64_t lse_part_stride, int parts,
                   int64_t rows, int head_dim, void* out, int out_dtype, float* lse_out, void* stream) {
   fat::set_last_error("");

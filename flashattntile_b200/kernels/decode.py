@@ -22,10 +22,14 @@ queries raise ``NotImplementedError``.
 
 from __future__ import annotations
 
+import ctypes
+import threading
+
 import torch
 
 from .. import _config, _lib
-from ..paging import PagedKVCache, check_value_stats, validate_cache_values, validate_metadata
+from ..paging import (PagedKVCache, check_value_numbers, check_value_stats, validate_cache_values,
+                      validate_metadata)
 
 DEFAULT_CONFIG = {"split_k": 1, "num_warps": 4, "num_stages": 2}
 # Import compatibility with code written against the reference: this build has
@@ -136,17 +140,21 @@ def _aligned_q(q: torch.Tensor) -> torch.Tensor:
 
 
 def prepare_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
-                   k_scale=None, v_scale=None, out=None, out_dtype=None, lse=None):
+                   k_scale=None, v_scale=None, out=None, out_dtype=None, lse=None, remember=False):
     """All of :func:`launch_decode`'s host work (checks, output, scratch, the
-    argument list) without the launch: returns a callable that launches on the
+    argument struct) without the launch: returns a callable that launches on the
     stream current now and returns the output.  Callers that must synchronise
     before launching (value checks) prepare first, so the GPU waits for no host
     work after the synchronisation.
+
+    ``remember``: keep the argument struct for the op fast path when nothing was
+    copied on the way (see ``_fast_decode``).
     """
     _require_cuda(q, k_cache, v_cache, page_table, seq_lens)
     lib = _lib.load()
     dev = q.device
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    q_in, table_in, lens_in, ks_in, vs_in = q, page_table, seq_lens, k_scale, v_scale
     q = _aligned_q(q)
     if k_cache.stride() != v_cache.stride():
         raise ValueError("k_cache and v_cache must have identical strides")
@@ -159,6 +167,7 @@ def prepare_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax
     batch, heads, dim = q.shape
     kvh = k_cache.shape[2]
     out_dtype = out_dtype or q.dtype
+    own_out = out is None
     if out is None:
         out = torch.empty((batch, heads, dim), dtype=out_dtype, device=dev)
     scale_stride = 0
@@ -166,33 +175,124 @@ def prepare_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax
         if k_scale.stride(1) != 1 or v_scale.stride() != k_scale.stride():
             k_scale, v_scale = k_scale.contiguous(), v_scale.contiguous()
         scale_stride = k_scale.stride(0)
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream_obj = torch.cuda.current_stream(dev)
+    stream = stream_obj.cuda_stream
     ws = _lib.workspace_for(idx, stream, dev, lib.fat_paged_decode_workspace_size(idx, batch, heads, kvh, dim))
     err = _lib.error_word_for(idx, stream, dev)
-    args = (q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
-            k_cache.stride(1), k_cache.stride(2), k_cache.shape[0], page_table.data_ptr(), page_table.stride(0),
-            page_table.shape[1], seq_lens.data_ptr(), _lib.ptr(k_scale), _lib.ptr(v_scale), scale_stride,
-            out.data_ptr(), out.stride(0), out.stride(1))
-    tail = (batch, heads, kvh, dim, int(page_size), _lib.DTYPE_CODE[q.dtype], _lib.DTYPE_CODE[k_cache.dtype],
-            _lib.DTYPE_CODE[out_dtype], float(softmax_scale), int(split_k), ws.data_ptr(), ws.numel(),
-            err.data_ptr(), stream)
-    if lse is None:
-        fn, args = lib.fat_paged_decode, args + tail
-    else:
+    if lse is not None:
         if lse.dtype != torch.float32 or lse.device != dev or lse.dim() != 2 or lse.stride(1) != 1 \
                 or tuple(lse.shape) != (batch, heads):
             raise ValueError(f"lse must be a float32 [{batch}, {heads}] tensor on {dev} with unit stride along heads")
-        fn, args = lib.fat_paged_decode_lse, args + (lse.data_ptr(), lse.stride(0)) + tail
+    call = _lib.DecodeCall(
+        q=q.data_ptr(), q_stride_b=q.stride(0), q_stride_h=q.stride(1), k_cache=k_cache.data_ptr(),
+        v_cache=v_cache.data_ptr(), kv_stride_page=k_cache.stride(0), kv_stride_slot=k_cache.stride(1),
+        kv_stride_head=k_cache.stride(2), num_pages=k_cache.shape[0], page_table=page_table.data_ptr(),
+        page_table_stride=page_table.stride(0), max_pages=page_table.shape[1], seq_lens=seq_lens.data_ptr(),
+        k_scale=_lib.ptr(k_scale), v_scale=_lib.ptr(v_scale), scale_stride_page=scale_stride, out=out.data_ptr(),
+        out_stride_b=out.stride(0), out_stride_h=out.stride(1), lse=_lib.ptr(lse),
+        lse_stride_b=0 if lse is None else lse.stride(0), batch=batch, num_heads=heads, num_kv_heads=kvh,
+        head_dim=dim, page_size=int(page_size), q_dtype=_lib.DTYPE_CODE[q.dtype],
+        kv_dtype=_lib.DTYPE_CODE[k_cache.dtype], out_dtype=_lib.DTYPE_CODE[out_dtype],
+        softmax_scale=float(softmax_scale), split_k_hint=int(split_k), workspace=ws.data_ptr(),
+        workspace_bytes=ws.numel(), error_word=err.data_ptr(), stream=stream, stats_out=None, stats_scratch=None)
+    fn = lib.fat_paged_decode_call
+
     def fire() -> torch.Tensor:
+        # `call` itself (not just its address) lives in this closure: the struct
+        # must outlive prepare_decode until the library has read it.
         if idx == torch.cuda.current_device():
-            status = fn(*args)
+            status = fn(ctypes.addressof(call))
         else:
             with torch.cuda.device(idx):
-                status = fn(*args)
+                status = fn(ctypes.addressof(call))
         _lib.check(status, "paged_decode")
         return out
 
+    if (remember and own_out and lse is None and q is q_in and page_table is table_in and seq_lens is lens_in
+            and k_scale is ks_in and v_scale is vs_in and idx == torch.cuda.current_device()):
+        _remember(_fast_key(q_in, k_cache, v_cache, table_in, lens_in, page_size, softmax_scale, split_k, ks_in,
+                            vs_in), call, out, ws, idx, stream, stream_obj, k_cache.shape[0],
+                  table_in.shape[1] * int(page_size))
     return fire
+
+
+# --------------------------------------------------------------------------- fast path
+# A serving loop calls the op with the same tensors (same storage, shapes,
+# strides, dtypes, stream) step after step.  After one call has passed every
+# structural check, its argument struct is kept under a key made of exactly
+# those properties; the next call with an equal key skips the checks and the
+# argument packing, allocates its output, runs the value checks (the
+# statistics kernel is queued in the same library call) and launches.  Entries
+# hold pointers and sizes only, never tensors, so they keep no memory alive;
+# the scratch buffer is re-checked on every hit.
+_FAST: dict = {}
+_FAST_MAX = 256
+
+
+class _Plan:
+    __slots__ = ("call", "addr", "out_shape", "out_dtype", "device", "ws_key", "ws_ptr", "stream_obj", "stats_host",
+                 "stats_host_ptr", "stats_dev_ptr", "stats_event", "num_pages", "capacity")
+
+
+def _fast_key(q, k, v, table, lens, page_size, scale, split_k, k_scale=None, v_scale=None):
+    dev = q.get_device()
+    if dev < 0:
+        return None
+    key = (threading.get_ident(), dev, torch._C._cuda_getCurrentRawStream(dev), q.data_ptr(), q.shape, q.stride(),
+           q.dtype, k.data_ptr(), k.shape, k.stride(), k.dtype, v.data_ptr(), v.shape, v.stride(), v.dtype,
+           table.data_ptr(), table.shape, table.stride(), table.dtype, table.get_device(), lens.data_ptr(),
+           lens.shape, lens.stride(), lens.dtype, lens.get_device(), int(page_size), float(scale), int(split_k))
+    if k_scale is not None:
+        key += (k_scale.data_ptr(), k_scale.shape, k_scale.stride(), k_scale.dtype, v_scale.data_ptr(),
+                v_scale.shape, v_scale.stride(), v_scale.dtype)
+    return key
+
+
+def _remember(key, call, out, ws, idx, stream, stream_obj, num_pages, capacity) -> None:
+    if key is None:
+        return
+    plan = _Plan()
+    plan.call, plan.addr = call, ctypes.addressof(call)
+    plan.out_shape, plan.out_dtype, plan.device = tuple(out.shape), out.dtype, out.device
+    plan.ws_key, plan.ws_ptr = (idx, stream), ws.data_ptr()
+    plan.stream_obj = stream_obj
+    scratch, host, event = _lib.stats_buffers(idx, stream, out.device)
+    if event.cuda_event == 0:
+        event.record(stream_obj)  # creates the CUDA event, whose handle the library records
+    plan.stats_host, plan.stats_host_ptr, plan.stats_dev_ptr, plan.stats_event = host, host.data_ptr(), \
+        scratch.data_ptr(), event
+    plan.num_pages, plan.capacity = int(num_pages), int(capacity)
+    if len(_FAST) >= _FAST_MAX:
+        _FAST.clear()
+    _FAST[key] = plan
+
+
+def _fast_decode(key) -> torch.Tensor | None:
+    """Launch a remembered decode (value checks included); None when there is no usable entry."""
+    plan = _FAST.get(key) if key is not None else None
+    if plan is None:
+        return None
+    ws = _lib._WS.get(plan.ws_key)
+    if ws is None or ws.data_ptr() != plan.ws_ptr or plan.device.index != torch.cuda.current_device():
+        return None
+    out = torch.empty(plan.out_shape, dtype=plan.out_dtype, device=plan.device)
+    call = plan.call
+    call.out = out.data_ptr()
+    checks = _config.validate_values()
+    if checks:
+        # The library queues the statistics, records the event, then the decode:
+        # the host waits for the 16-byte statistics only, never for the decode.
+        call.stats_out, call.stats_scratch = plan.stats_host_ptr, plan.stats_dev_ptr
+        call.stats_event = plan.stats_event.cuda_event
+    else:
+        call.stats_out = call.stats_scratch = call.stats_event = None
+    status = _lib.load().fat_paged_decode_call(plan.addr)
+    _lib.check(status, "paged_decode")
+    if checks:
+        plan.stats_event.synchronize()
+        lo, _ = check_value_numbers(plan.stats_host.tolist(), plan.capacity, plan.num_pages)
+        _check_lengths((lo, None))
+    return out
 
 
 def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k=1,
@@ -210,9 +310,34 @@ def launch_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_
                           k_scale=k_scale, v_scale=v_scale, out=out, out_dtype=out_dtype, lse=lse)()
 
 
+def _fast_args(q, cache, softmax_scale, config):
+    """(scale, split_k) when this call may take the fast path, else None."""
+    if type(cache) is not PagedKVCache or not isinstance(q, torch.Tensor) or q.dim() != 3:
+        return None
+    if config is None:
+        split_k = 1
+    elif type(config) is dict and len(config) == 1 and type(config.get("split_k")) is int:
+        split_k = config["split_k"]
+    else:
+        return None
+    if softmax_scale is None:
+        scale = q.shape[-1] ** -0.5
+    elif isinstance(softmax_scale, (int, float)):
+        scale = float(softmax_scale)
+    else:
+        return None
+    return scale, split_k
+
+
 def paged_decode_attention(q: torch.Tensor, cache: PagedKVCache, softmax_scale: float | None = None,
                            config: dict | None = None, grouped: bool = False) -> torch.Tensor:
     """One query per sequence against a paged fp16/bf16 cache -> ``[B, H, D]`` in q's dtype."""
+    fast = _fast_args(q, cache, softmax_scale, config)
+    if fast is not None:
+        out = _fast_decode(_fast_key(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens,
+                                     cache.page_size, *fast))
+        if out is not None:
+            return out
     _check_decode_structure(q, cache)
     del grouped  # every launch shares each K/V page across its GQA group
     try:
@@ -224,7 +349,7 @@ def paged_decode_attention(q: torch.Tensor, cache: PagedKVCache, softmax_scale: 
         if cache.k_cache.dtype != q.dtype:
             raise ValueError(f"q dtype {q.dtype} must match cache dtype {cache.k_cache.dtype}")
         fire = prepare_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens,
-                              cache.page_size, scale, cfg["split_k"])
+                              cache.page_size, scale, cfg["split_k"], remember=True)
     except Exception:
         _value_checks(cache)  # the reference reports bad cache values first
         raise
@@ -234,6 +359,13 @@ def paged_decode_attention(q: torch.Tensor, cache: PagedKVCache, softmax_scale: 
 def paged_decode_attention_fp8(q: torch.Tensor, cache: PagedKVCache, scales, softmax_scale: float | None = None,
                                config: dict | None = None) -> torch.Tensor:
     """Decode against an INT8 / float8_e4m3fn cache with per-(page, KV-head) fp32 scales."""
+    fast = _fast_args(q, cache, softmax_scale, config)
+    if fast is not None and isinstance(scales, dict) and isinstance(scales.get("k"), torch.Tensor) \
+            and isinstance(scales.get("v"), torch.Tensor):
+        out = _fast_decode(_fast_key(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens,
+                                     cache.page_size, *fast, scales["k"], scales["v"]))
+        if out is not None:
+            return out
     _check_decode_structure(q, cache)
     try:
         fire = _prepare_decode_fp8(q, cache, scales, softmax_scale, config)
@@ -257,4 +389,4 @@ def _prepare_decode_fp8(q, cache, scales, softmax_scale, config):
     if q.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError(f"quantised decode requires fp16/bf16 queries, got {q.dtype}")
     return prepare_decode(q, cache.k_cache, cache.v_cache, cache.page_table, cache.seq_lens, cache.page_size,
-                          scale, cfg["split_k"], k_scale=k_scale.float(), v_scale=v_scale.float())
+                          scale, cfg["split_k"], k_scale=k_scale.float(), v_scale=v_scale.float(), remember=True)

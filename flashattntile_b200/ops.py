@@ -22,7 +22,7 @@ from __future__ import annotations
 
 import torch
 
-from .kernels.decode import paged_decode_attention, paged_decode_attention_fp8
+from .kernels.decode import _fast_decode, _fast_key, paged_decode_attention, paged_decode_attention_fp8
 from .kernels.prefill import prefill_attention
 from .paging import PagedKVCache
 
@@ -45,6 +45,10 @@ _LIB.define("prefill_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens_q, T
 
 def _paged_decode_cuda(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
                        seq_lens: torch.Tensor, page_size: int, softmax_scale: float, split_k: int) -> torch.Tensor:
+    # Steps after the first with the same tensors skip the structural checks (_fast_decode).
+    out = _fast_decode(_fast_key(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k))
+    if out is not None:
+        return out
     cache = PagedKVCache(k_cache=k_cache, v_cache=v_cache, page_table=page_table, seq_lens=seq_lens,
                          page_size=int(page_size))
     return paged_decode_attention(q, cache, softmax_scale=softmax_scale, config={"split_k": int(split_k)})
@@ -53,6 +57,10 @@ def _paged_decode_cuda(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
 def _paged_decode_quant_cuda(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: torch.Tensor,
                              v_scale: torch.Tensor, page_table: torch.Tensor, seq_lens: torch.Tensor, page_size: int,
                              softmax_scale: float, split_k: int) -> torch.Tensor:
+    out = _fast_decode(_fast_key(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax_scale, split_k,
+                                 k_scale, v_scale))
+    if out is not None:
+        return out
     cache = PagedKVCache(k_cache=k_cache, v_cache=v_cache, page_table=page_table, seq_lens=seq_lens,
                          page_size=int(page_size))
     return paged_decode_attention_fp8(q, cache, {"k": k_scale, "v": v_scale}, softmax_scale=softmax_scale,

@@ -147,12 +147,17 @@ def validate_cache_values(cache: PagedKVCache, *, check_pages: bool = True) -> t
 
 def check_value_stats(cache: PagedKVCache, stats, *, check_pages: bool = True) -> tuple[int, int]:
     """The assertions of the value checks on ``cache_value_stats`` numbers."""
+    return check_value_numbers(stats, cache.capacity, cache.num_pages, check_pages=check_pages)
+
+
+def check_value_numbers(stats, capacity: int, num_pages: int, *, check_pages: bool = True) -> tuple[int, int]:
+    """:func:`check_value_stats` on plain numbers (the cache's capacity and page count)."""
     lo, max_len, umin, umax = (int(x) for x in stats)
     _assert(lo >= 0, "seq_lens must be non-negative")
-    _assert(max_len <= cache.capacity, f"seq_len {max_len} exceeds page-table capacity {cache.capacity}")
+    _assert(max_len <= capacity, f"seq_len {max_len} exceeds page-table capacity {capacity}")
     if check_pages and max_len > 0:
         _assert(umin >= 0, "page_table contains a negative page id")
-        _assert(umax < cache.num_pages, f"page_table references page {umax} but cache has {cache.num_pages} pages")
+        _assert(umax < num_pages, f"page_table references page {umax} but cache has {num_pages} pages")
     return lo, max_len
 
 

@@ -137,6 +137,47 @@ int fat_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, cons
                      int32_t* error_word, void* stream);
 
 /*
+ * fat_paged_decode_lse's arguments in one struct, for callers that keep them
+ * between calls (an op whose tensors stay put from step to step pays the
+ * argument conversion once and changes only `out`).  With `stats_out` set,
+ * the call first queues fat_cache_value_stats(seq_lens, page_table, ...,
+ * stats_scratch, stats_out) on the same stream (and records `stats_event`
+ * after it), so value checks and decode cost one crossing; `lse` may be NULL.  Same status codes and device error
+ * word as fat_paged_decode.  No reference counterpart (a calling convention).
+ */
+typedef struct fat_decode_call {
+  const void* q;
+  int64_t q_stride_b, q_stride_h;
+  const void* k_cache;
+  const void* v_cache;
+  int64_t kv_stride_page, kv_stride_slot, kv_stride_head, num_pages;
+  const int32_t* page_table;
+  int64_t page_table_stride, max_pages;
+  const int32_t* seq_lens;
+  const float* k_scale;
+  const float* v_scale;
+  int64_t scale_stride_page;
+  void* out;
+  int64_t out_stride_b, out_stride_h;
+  float* lse;
+  int64_t lse_stride_b;
+  int32_t batch, num_heads, num_kv_heads, head_dim, page_size;
+  int32_t q_dtype, kv_dtype, out_dtype;
+  float softmax_scale;
+  int32_t split_k_hint;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* error_word;
+  void* stream;
+  int32_t* stats_out;      /* optional: 4 int32 (pinned host or device), see fat_cache_value_stats */
+  int32_t* stats_scratch;  /* 4 int32 on the device, used with stats_out */
+  void* stats_event;       /* optional cudaEvent_t, recorded on `stream` right after the statistics: a
+                              host that waits on it to check the values does not wait for the decode */
+} fat_decode_call;
+
+int fat_paged_decode_call(const fat_decode_call* call);
+
+/*
  * fat_paged_decode that also writes, per (sequence, query head), the base-2
  * log-sum-exp of the scaled scores, lse[b * lse_stride_b + h] = m + log2(l)
  * (-inf for a sequence with no cached tokens).  With out_dtype F32 the pair

@@ -112,3 +112,32 @@ def test_decode_loop_has_no_cpu_path():
     cache = PagedKVCache(k, k.clone(), torch.zeros(1, 4, dtype=torch.int32), torch.zeros(1, dtype=torch.int32), 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         DecodeLoop(cache, num_heads=4)
+
+
+def test_decode_call_struct_matches_the_header():
+    """The ctypes mirror of ``fat_decode_call`` has the C struct's size and field offsets."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    from flashattntile_b200 import _lib
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    fields = [name for name, _ in _lib.DecodeCall._fields_]
+    root = Path(__file__).resolve().parents[1]
+    src = "#include <stdio.h>\n#include <stddef.h>\n#include \"flashattn_tile_b200.h\"\nint main(void) {\n"
+    src += '  printf("%zu\\n", sizeof(fat_decode_call));\n'
+    for f in fields:
+        src += f'  printf("%zu\\n", offsetof(fat_decode_call, {f}));\n'
+    src += "  return 0;\n}\n"
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = Path(d) / "layout.c", Path(d) / "layout"
+        c.write_text(src)
+        subprocess.run([gcc, "-I", str(root / "include"), str(c), "-o", str(exe)], check=True)
+        values = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    import ctypes
+
+    assert values[0] == ctypes.sizeof(_lib.DecodeCall)
+    assert values[1:] == [getattr(_lib.DecodeCall, f).offset for f in fields]
