@@ -143,7 +143,10 @@ __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int c
 
 // kPaged: K/V come from a paged cache through the page table (4-D maps
 // {head_dim, kv head, slot, page}); otherwise from packed [tokens, heads, dim].
-template <typename T, int D, bool kPaged>
+// kSplit: this instantiation can feed P as head + remainder (p_split 1 and 2).
+// The other one is the plain kernel, without the split code in its softmax loop
+// (compiled apart: the branch alone cost 13% in the common path).
+template <typename T, int D, bool kPaged, bool kSplit>
 __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -388,12 +391,14 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       // accumulated on top (votes are visible: p_full's arrivals release them).
       auto issue_p = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t loV, int jj, int t) {
         issue_pv(d_tmem, a_tmem, loV, jj > 0 ? 1u : 0u);
-        bool split = p.p_split == 2;
-        if (p.p_split == 1) {
-          const volatile int* v = votes + t * 8 + (jj & 1);
-          split = (v[0] | v[2] | v[4] | v[6]) != 0;
+        if constexpr (kSplit) {
+          bool split = p.p_split == 2;
+          if (p.p_split == 1) {
+            const volatile int* v = votes + t * 8 + (jj & 1);
+            split = (v[0] | v[2] | v[4] | v[6]) != 0;
+          }
+          if (split) issue_pv(d_tmem, a_tmem + BN / 2, loV, 1u);
         }
-        if (split) issue_pv(d_tmem, a_tmem + BN / 2, loV, 1u);
       };
       int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0;
       // Failure-path test: a wait that nothing ends runs out after p.wait_ns and
@@ -529,53 +534,93 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       }
       const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
       float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-      // Probabilities in place of the scores.
-#pragma unroll
-      for (int i = 0; i < BN; i += 4) {
-        float x0, x1, x2, x3;
-        fma2(x0, x1, s[i], s[i + 1], p.scale_log2, -msub);
-        fma2(x2, x3, s[i + 2], s[i + 3], p.scale_log2, -msub);
-        s[i] = fast_exp2(x0);
-        s[i + 1] = fast_exp2(x1);
-        s[i + 2] = fast_exp2(x2);
-        s[i + 3] = fast_exp2(x3);
-        add2(sum0, sum1, s[i], s[i + 1]);
-        add2(sum2, sum3, s[i + 2], s[i + 3]);
-      }
-      l_sum += (sum0 + sum1) + (sum2 + sum3);
-      bool split = p.p_split == 2;
-      if (p.p_split == 1) split = __any_sync(0xffffffffu, fast_exp2(mx - msub) > kSplitTheta * l_sum);
-      if (!split) {
+      if constexpr (!kSplit) {
         // P rounded to the input dtype (prefill.py:128), packed over S's first 64 columns.
 #pragma unroll
         for (int c = 0; c < BN / 64; ++c) {
           uint32_t packed[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) packed[i] = pack2<T>(s[64 * c + 2 * i], s[64 * c + 2 * i + 1]);
+          for (int i = 0; i < 32; i += 2) {
+            float x0, x1, x2, x3;
+            fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
+            fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
+            const float p0 = fast_exp2(x0);
+            const float p1 = fast_exp2(x1);
+            const float p2 = fast_exp2(x2);
+            const float p3 = fast_exp2(x3);
+            add2(sum0, sum1, p0, p1);
+            add2(sum2, sum3, p2, p3);
+            packed[i] = pack2<T>(p0, p1);
+            packed[i + 1] = pack2<T>(p2, p3);
+          }
           tc::st32(lane_base + colS + 32 * c, packed);
         }
-        if (p.p_split == 1) {
-          // Another warp of this tile may vote to split: the remainder pass then
-          // reads these rows' columns [64, 128), which must hold zeros.
-          uint32_t zero[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) zero[i] = 0u;
-          tc::st32(lane_base + colS + BN / 2, zero);
-          tc::st32(lane_base + colS + BN / 2 + 32, zero);
-        }
+        l_sum += (sum0 + sum1) + (sum2 + sum3);
       } else {
-        // Head in columns [0, 64), remainder p - head in [64, 128): every score
-        // of this S row is already in registers, so those columns are free.
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) split_hi_lo<T>(s[32 * c + 2 * i], s[32 * c + 2 * i + 1], hi[i], lo[i]);
-          tc::st16(lane_base + colS + 16 * c, hi);
-          tc::st16(lane_base + colS + BN / 2 + 16 * c, lo);
+        // Decided before the exponentials: the row's sum after this tile is at
+        // least its sum so far plus the tile's largest p, so a key of an unsplit
+        // tile still ends with weight <= kSplitTheta.
+        bool split = p.p_split == 2;
+        if (p.p_split == 1) {
+          const float pmax = fast_exp2(mx - msub);
+          split = __any_sync(0xffffffffu, pmax > kSplitTheta * (l_sum + pmax));
         }
+        if (!split) {
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c) {
+            uint32_t packed[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              float x0, x1, x2, x3;
+              fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
+              fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
+              const float p0 = fast_exp2(x0);
+              const float p1 = fast_exp2(x1);
+              const float p2 = fast_exp2(x2);
+              const float p3 = fast_exp2(x3);
+              add2(sum0, sum1, p0, p1);
+              add2(sum2, sum3, p2, p3);
+              packed[i] = pack2<T>(p0, p1);
+              packed[i + 1] = pack2<T>(p2, p3);
+            }
+            tc::st32(lane_base + colS + 32 * c, packed);
+          }
+          if (p.p_split == 1) {
+            // Another warp of this tile may vote to split: the remainder pass then
+            // reads these rows' columns [64, 128), which must hold zeros.
+            uint32_t zero[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) zero[i] = 0u;
+            tc::st32(lane_base + colS + BN / 2, zero);
+            tc::st32(lane_base + colS + BN / 2 + 32, zero);
+          }
+        } else {
+          // Head in columns [0, 64), remainder p - head in [64, 128): every score
+          // of this S row is already in registers, so those columns are free.
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              float x0, x1, x2, x3;
+              fma2(x0, x1, s[32 * c + 2 * i], s[32 * c + 2 * i + 1], p.scale_log2, -msub);
+              fma2(x2, x3, s[32 * c + 2 * i + 2], s[32 * c + 2 * i + 3], p.scale_log2, -msub);
+              const float p0 = fast_exp2(x0);
+              const float p1 = fast_exp2(x1);
+              const float p2 = fast_exp2(x2);
+              const float p3 = fast_exp2(x3);
+              add2(sum0, sum1, p0, p1);
+              add2(sum2, sum3, p2, p3);
+              split_hi_lo<T>(p0, p1, hi[i], lo[i]);
+              split_hi_lo<T>(p2, p3, hi[i + 1], lo[i + 1]);
+            }
+            tc::st16(lane_base + colS + 16 * c, hi);
+            tc::st16(lane_base + colS + BN / 2 + 16 * c, lo);
+          }
+        }
+        l_sum += (sum0 + sum1) + (sum2 + sum3);
+        if (p.p_split == 1 && lane == 0) votes[t * 8 + (warp & 3) * 2 + (j & 1)] = split ? 1 : 0;
       }
-      if (p.p_split == 1 && lane == 0) votes[t * 8 + (warp & 3) * 2 + (j & 1)] = split ? 1 : 0;
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(pbar);
@@ -703,7 +748,8 @@ int encode_out_map(const PrefillArgs& a, const CUtensorMap& placeholder, CUtenso
 template <typename T, int D>
 int launch_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
-  auto kern = pre::prefill_kernel<T, D, false>;
+  const int p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
+  auto kern = p_split != 0 ? pre::prefill_kernel<T, D, false, true> : pre::prefill_kernel<T, D, false, false>;
   static_assert(L::kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill)", e);
@@ -744,7 +790,7 @@ int launch_t(const PrefillArgs& a) {
   p.err = a.error_word;
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
-  p.p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
+  p.p_split = p_split;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
@@ -756,7 +802,8 @@ int launch_t(const PrefillArgs& a) {
 template <typename T, int D>
 int launch_paged_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
-  auto kern = pre::prefill_kernel<T, D, true>;
+  const int p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
+  auto kern = p_split != 0 ? pre::prefill_kernel<T, D, true, true> : pre::prefill_kernel<T, D, true, false>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill paged)", e);
   std::string why;
@@ -805,7 +852,7 @@ int launch_paged_t(const PrefillArgs& a) {
   p.seq_lens_k = a.seq_lens_k;
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
-  p.p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
+  p.p_split = p_split;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
