@@ -499,6 +499,17 @@ def run_comparators(device, args, peaks) -> dict:
 
     record("cfg2_decode_ours", lambda: launch_decode(q, k, v, table, lens, c["page_size"], scale, 1, out=out),
            ours, nbytes, "GB/s")
+    # The reference's own CUDA C++ decode (csrc/paged_decode.cu), built for sm_100a by oracle/build_ref_native.py.
+    try:
+        from oracle import build_ref_native
+
+        native = build_ref_native.load_module()
+        if native is None:
+            raise RuntimeError("oracle/_ref holds no build of the reference's native kernel")
+        record("cfg2_decode_reference_native_cuda", lambda: native.paged_decode(q, k, v, table, lens, c["page_size"],
+                                                                                 scale), ours, nbytes, "GB/s")
+    except Exception as e:
+        res["cfg2_decode_reference_native_cuda"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
     try:
         import flashinfer
 
@@ -560,6 +571,23 @@ def run_comparators(device, args, peaks) -> dict:
                ref3, flops, "TFLOP/s")
     except Exception as e:
         res["cfg3_prefill_flash_attn2"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    del sets, ref3, o3
+    torch.cuda.empty_cache()
+    # The reference's Triton kernels (cfg2 decode at split_k 1/2/4/8, cfg3 prefill), in a process of their own.
+    import subprocess
+
+    ref_dir = ROOT / "baseline" / "_ref"
+    if (ref_dir / "flashattn_tile").is_dir():
+        run = subprocess.run([sys.executable, str(ROOT / "tests" / "ref_triton_runner.py"), str(ref_dir), "time",
+                              str(steps), str(args.warmup)], capture_output=True, text=True, timeout=900,
+                             env=dict(os.environ, PYTHONPATH=str(ROOT)))
+        lines = [ln for ln in run.stdout.splitlines() if ln.startswith("{")]
+        if run.returncode == 0 and lines:
+            res.update(json.loads(lines[-1]))
+        else:
+            res["reference_triton"] = {"unavailable": (run.stderr or run.stdout)[-300:]}
+    else:
+        res["reference_triton"] = {"unavailable": "the reference is not installed under baseline/_ref"}
     return res
 
 
