@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
     "fat_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "fat_expire_next_waits": (None, [_i32]),
     "fat_set_prefill_p_split": (_i32, [_i32]),
+    "fat_set_prefill_schedule": (_i32, [_i32]),
     "fat_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "fat_paged_decode": (
         _i32,

@@ -30,6 +30,15 @@ int fat_set_prefill_p_split(int mode) {
   return fat::set_prefill_p_split(mode);
 }
 
+int fat_set_prefill_schedule(int mode) {
+  if (mode < 0 || mode > 1) {
+    fat::set_last_error("prefill schedule must be 0 or 1, got " + std::to_string(mode));
+    return -2;
+  }
+  fat::set_last_error("");
+  return fat::set_prefill_schedule(mode);
+}
+
 size_t fat_paged_decode_workspace_size(int device, int batch, int num_heads, int num_kv_heads, int head_dim) {
   return fat::decode_workspace_bytes(device, batch, num_heads, num_kv_heads, head_dim);
 }

@@ -36,7 +36,11 @@ namespace {
 std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
 std::atomic<int> g_expire_requests{0};
 std::atomic<int> g_p_split{-1};
+std::atomic<int> g_prefill_schedule{0};
 }  // namespace
+
+int set_prefill_schedule(int mode) { return g_prefill_schedule.exchange(mode, std::memory_order_relaxed); }
+int prefill_schedule() { return g_prefill_schedule.load(std::memory_order_relaxed); }
 
 int set_prefill_p_split(int mode) { return g_p_split.exchange(mode, std::memory_order_relaxed); }
 

@@ -39,6 +39,11 @@ void request_expiry(int n);
 int set_prefill_p_split(int mode);  // returns the previous setting
 int prefill_p_split(bool bf16);     // the mode a launch of that dtype uses
 
+// Prefill grid (fat_set_prefill_schedule): 0 persistent when every CTA's item
+// list fits (the default), 1 always one CTA per (head, sequence, query pair).
+int set_prefill_schedule(int mode);  // returns the previous setting
+int prefill_schedule();
+
 // The calling thread's current CUDA device, or -1 when there is none (no
 // device, or the runtime failed to report it).
 int current_device();

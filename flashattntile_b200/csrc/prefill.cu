@@ -35,6 +35,9 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <type_traits>
 
 #include "common.cuh"
@@ -50,6 +53,9 @@ constexpr int BN = 128;    // keys per K/V tile
 constexpr int kSoftmaxThreads = 128;  // per tile
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 without rescaling
+// Persistent grid: items in flight between the producer warp (which claims
+// and describes them) and the MMA issuer and softmax warps.
+constexpr int kItemSlots = 4;
 
 struct Params {
   const int* cu_q;
@@ -72,6 +78,8 @@ struct Params {
   unsigned long long wait_ns;  // limit of every bounded wait
   int expire;            // the MMA issuer first waits on a barrier phase nothing completes (failure-path tests)
   int p_split;           // P into P.V as head + remainder: 0 never, 1 where a key weighs (vote), 2 always
+  int batch, num_pairs;  // sequences; 2-tile query pairs of the longest sequence
+  int* sched;            // kPersist: {next rank, CTAs done}, zero at launch and zeroed again by the last CTA
 };
 
 // p_split == 1: a key tile of a query tile enters P.V as a 16-bit head plus a
@@ -107,9 +115,11 @@ struct Layout {
   static constexpr int kStagesK = D <= 64 ? 4 : (D <= 128 ? 3 : 1);
   static constexpr int kStagesV = D <= 64 ? 4 : (D <= 128 ? 2 : 1);
   // q_full, K and V full/empty rings, s_full and p_full per tile, drain, vtail,
-  // never; then the tensor-memory slot, the abort flag and the split votes
-  // ([tile][warp][parity] ints).
-  static constexpr int kBarBytes = 8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 3) + 8 + 4 * 8 * kTiles;
+  // never, q_empty, item_full and item_empty per item slot; then the
+  // tensor-memory slot, the abort flag, the split votes ([tile][warp][parity]
+  // ints) and the item slots (8 ints each).
+  static constexpr int kBarBytes =
+      8 * (1 + 2 * kStagesK + 2 * kStagesV + 2 * kTiles + 4 + 2 * kItemSlots) + 8 + 4 * 8 * kTiles + 32 * kItemSlots;
   static constexpr size_t kSmem = 1024 + size_t(kTile) * (kTiles + kStagesK + kStagesV) + kBarBytes;
   static_assert(kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
   static constexpr uint32_t kColS = 0;               // S_t at column kColS + 128 t
@@ -141,12 +151,124 @@ __device__ __forceinline__ int tiles_needed(int m0, int q_len, int kv_len, int c
   return lim < 0 ? 0 : min(n_kv, lim / BN + 1);
 }
 
+// One work item: query pair `pair` (rows [256 pair, 256 pair + 256) with two
+// tiles) of head h of sequence b, and the K/V tiles each of its tiles needs.
+struct Work {
+  int b, h, kvh, q0, q_len, k0, kv_len, m0, offset, n0, n1, n_max, q_tiles;
+};
+
+// The tile counts of an item whose sequence fields are set.
+template <int kTiles>
+__device__ __forceinline__ void finish_work(const Params& p, int pair, Work& w) {
+  w.kvh = w.h / p.group;
+  w.m0 = pair * BM * kTiles;
+  w.offset = w.kv_len - w.q_len;  // bottom-right causal alignment
+  w.n0 = tiles_needed(w.m0, w.q_len, w.kv_len, p.causal);
+  w.n1 = kTiles > 1 ? tiles_needed(w.m0 + BM, w.q_len, w.kv_len, p.causal) : 0;
+  w.n_max = max(w.n0, w.n1);
+  w.q_tiles = (kTiles > 1 && w.m0 + BM < w.q_len) ? 2 : 1;
+}
+
+template <int kTiles, bool kPaged>
+__device__ __forceinline__ Work describe_work(const Params& p, int b, int h, int pair) {
+  Work w;
+  w.b = b;
+  w.h = h;
+  w.q0 = __ldg(p.cu_q + b);
+  w.q_len = __ldg(p.cu_q + b + 1) - w.q0;
+  w.k0 = kPaged ? 0 : __ldg(p.cu_k + b);
+  // Paged: a length past the page table is cut to its capacity (and reported),
+  // so tile positions stay in 32 bits and inside the table.
+  w.kv_len = kPaged ? min(__ldg(p.seq_lens_k + b), p.cap_tokens) : __ldg(p.cu_k + b + 1) - w.k0;
+  finish_work<kTiles>(p, pair, w);
+  return w;
+}
+
+// An item as the producer warp publishes it: {b (-1: no more items), h, pair,
+// q0, q_len, k0, kv_len}.
+template <int kTiles>
+__device__ __forceinline__ Work work_from_slot(const Params& p, const volatile int* e) {
+  Work w;
+  w.b = e[0];
+  w.h = e[1];
+  w.q0 = e[3];
+  w.q_len = e[4];
+  w.k0 = e[5];
+  w.kv_len = e[6];
+  finish_work<kTiles>(p, e[2], w);
+  return w;
+}
+
+__device__ __forceinline__ void write_slot(volatile int* d, const Work& w, int pair, bool have) {
+  d[0] = have ? w.b : -1;
+  d[1] = w.h;
+  d[2] = pair;
+  d[3] = w.q0;
+  d[4] = w.q_len;
+  d[5] = w.k0;
+  d[6] = w.kv_len;
+}
+
+// Persistent grid: the live items in one global order -- query pair index
+// descending (for causal attention the heaviest items first), then sequence,
+// then head -- are claimed one at a time from a counter, so CTAs that finish
+// early take more.  A CTA's claimed ranks only grow, so it maps them to items
+// with a cursor that only moves forward: the pair holding the rank, and within
+// it the scan position over the sequences long enough for that pair.
+struct ItemCursor {
+  int pr;               // pair of the ranks [base, end)
+  long long base, end;
+  int bscan, seen;      // next 32-sequence chunk of pair pr to scan; live sequences before it
+};
+
+template <int kTiles>
+__device__ __forceinline__ bool seq_reaches(const Params& p, int b, int m0) {
+  return b < p.batch && __ldg(p.cu_q + b + 1) - __ldg(p.cu_q + b) > m0;
+}
+
+// Map rank r (no smaller than any rank this cursor mapped before) to its item;
+// false once r lies past the last live item.  Run by one whole warp.
+template <int kTiles>
+__device__ bool cursor_map(const Params& p, ItemCursor& c, long long r, int lane, int& b, int& h, int& pair) {
+  constexpr int kRows = BM * kTiles;
+  while (r >= c.end) {
+    if (--c.pr < 0) return false;
+    const int m0 = c.pr * kRows;
+    int n = 0;
+    for (int b0 = 0; b0 < p.batch; b0 += 32)
+      n += __popc(__ballot_sync(0xffffffffu, seq_reaches<kTiles>(p, b0 + lane, m0)));
+    c.base = c.end;
+    c.end = c.base + (long long)n * p.num_heads;
+    c.bscan = 0;
+    c.seen = 0;
+  }
+  const long long i = r - c.base;
+  const int want = int(i / p.num_heads);
+  h = int(i - (long long)want * p.num_heads);
+  pair = c.pr;
+  const int m0 = c.pr * kRows;
+  for (; c.bscan < p.batch; c.bscan += 32) {
+    const bool lv = seq_reaches<kTiles>(p, c.bscan + lane, m0);
+    const unsigned m = __ballot_sync(0xffffffffu, lv);
+    if (c.seen + __popc(m) > want) {
+      const unsigned hit = __ballot_sync(0xffffffffu, lv && c.seen + __popc(m & ((1u << lane) - 1u)) == want);
+      b = c.bscan + __ffs(hit) - 1;
+      return true;
+    }
+    c.seen += __popc(m);
+  }
+  return false;  // not reached: want < the pair's live count
+}
+
 // kPaged: K/V come from a paged cache through the page table (4-D maps
 // {head_dim, kv head, slot, page}); otherwise from packed [tokens, heads, dim].
 // kSplit: this instantiation can feed P as head + remainder (p_split 1 and 2).
+// kPersist: one CTA per SM claiming items (rounded P only: the split kernel's
+// softmax and issuer need every register they have, and its per-item build runs
+// faster); otherwise one CTA per item.
 // The other one is the plain kernel, without the split code in its softmax loop
 // (compiled apart: the branch alone cost 13% in the common path).
-template <typename T, int D, bool kPaged, bool kSplit>
+template <typename T, int D, bool kPaged, bool kSplit, bool kPersist>
 __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -158,25 +280,6 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdescQK = tc::idesc_f16(BM, BN, fmt, 0, 0);
   constexpr uint32_t kIdescPV = tc::idesc_f16(BM, D, fmt, 0, 1);
-
-  const int h = blockIdx.x % p.num_heads;
-  const int b = blockIdx.x / p.num_heads;
-  const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
-  const int q0 = __ldg(p.cu_q + b), q_len = __ldg(p.cu_q + b + 1) - q0;
-  const int k0 = kPaged ? 0 : __ldg(p.cu_k + b);
-  // Paged: a length past the page table is cut to its capacity (and reported),
-  // so tile positions stay in 32 bits and inside the table.
-  const int raw_kv = kPaged ? __ldg(p.seq_lens_k + b) : 0;
-  const int kv_len = kPaged ? min(raw_kv, p.cap_tokens) : __ldg(p.cu_k + b + 1) - k0;
-  if (kPaged && raw_kv > p.cap_tokens && threadIdx.x == 0) raise_error(p.err, FAT_DEVERR_BAD_LENGTH);
-  const int m0 = pair * kRowsPerCta;
-  if (m0 >= q_len) return;  // uniform for the CTA, before any barrier or allocation
-  const int kvh = h / p.group;
-  const int offset = kv_len - q_len;  // bottom-right causal alignment
-  const int n0 = tiles_needed(m0, q_len, kv_len, p.causal);
-  const int n1 = kTiles > 1 ? tiles_needed(m0 + BM, q_len, kv_len, p.causal) : 0;
-  const int n_max = max(n0, n1);
-  const int q_tiles = (kTiles > 1 && m0 + BM < q_len) ? 2 : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -191,18 +294,35 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   const uint32_t v_full = k_empty + 8 * SK;  // [SV]
   const uint32_t v_empty = v_full + 8 * SV;  // [SV]
   const uint32_t s_full = v_empty + 8 * SV;  // [kTiles]: S_t(j) complete (and every earlier MMA)
-  const uint32_t p_full = s_full + 8 * kTiles;  // [kTiles]: P_t(j) written, O_t rescaled
+  const uint32_t p_full = s_full + 8 * kTiles;  // [kTiles]: P_t(j) written, O_t rescaled; or O_t seen final
   const uint32_t drain = p_full + 8 * kTiles;   // every MMA of the CTA complete
   const uint32_t vtail = drain + 8;             // paged: a partly valid V tile landed (before zeroing its tail)
   const uint32_t never = vtail + 8;             // initialised, never arrived on (failure-path tests)
+  const uint32_t q_empty = never + 8;           // an item's last Q.K^T completed: its Q buffers are free
+  const uint32_t item_full = q_empty + 8;                 // [kItemSlots]: the producer published an item
+  const uint32_t item_empty = item_full + 8 * kItemSlots;  // [kItemSlots]: every consumer is done with it
   volatile uint32_t* tmem_slot =
-      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 3);
+      reinterpret_cast<volatile uint32_t*>(bars + 1 + 2 * SK + 2 * SV + 2 * kTiles + 4 + 2 * kItemSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Split votes of the softmax warps, read by the MMA issuer after p_full:
   // [tile][warp of the warpgroup][key tile parity].
   volatile int* votes = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  // Published items (persistent grid): [slot][8] ints, see work_from_slot.
+  volatile int* slots = votes + 8 * kTiles;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // One CTA per item: this CTA's (sequence, head, pair).
+  const int own_b = blockIdx.x / p.num_heads, own_h = blockIdx.x % p.num_heads;
+  const int own_pair = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles start first
+  if (!kPersist) {
+    // Paged: a length past the page table is cut to its capacity (and reported),
+    // so tile positions stay in 32 bits and inside the table.
+    if (kPaged && tid == 0 && __ldg(p.seq_lens_k + own_b) > p.cap_tokens) raise_error(p.err, FAT_DEVERR_BAD_LENGTH);
+    if (own_pair * kRowsPerCta >= __ldg(p.cu_q + own_b + 1) - __ldg(p.cu_q + own_b)) return;  // before any barrier
+    // The item goes to slot 0 now, so no role waits on these loads after the barrier setup.
+    if (tid == 0) write_slot(slots, describe_work<kTiles, kPaged>(p, own_b, own_h, own_pair), own_pair, true);
+  }
+
   if (warp == kMmaWarp) {
     tc::tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
     tc::tmem_relinquish();
@@ -224,6 +344,11 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     mbar_init(drain, 1);
     mbar_init(vtail, 1);
     mbar_init(never, 1);
+    mbar_init(q_empty, 1);
+    for (int e = 0; e < kItemSlots; ++e) {
+      mbar_init(item_full + 8 * e, 1);
+      mbar_init(item_empty + 8 * e, 1 + 4 * kTiles);  // the MMA issuer and every softmax warp
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -231,135 +356,201 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // Item k as the consumers (MMA issuer, softmax warps) see it: the CTA's own
+  // item (one CTA per item, k == 0 only), or ring slot k % kItemSlots once the
+  // producer has published it.  False when there is no item k (or a wait failed).
+  auto consumer_item = [&](int k, Work& w, bool& ok) -> bool {
+    if (!kPersist) {
+      if (k > 0) return false;
+      w = work_from_slot<kTiles>(p, slots);
+      return true;
+    }
+    const int e = k % kItemSlots;
+    if (!mbar_wait_bounded(item_full + 8 * e, (k / kItemSlots) & 1, p.err, abort_flag, p.wait_ns)) {
+      ok = false;
+      return false;
+    }
+    if (slots[8 * e] < 0) return false;
+    w = work_from_slot<kTiles>(p, slots + 8 * e);
+    return true;
+  };
+  // The same item again, once consumer_item(k) returned it and before release_item(k).
+  auto peek_item = [&](int k) { return work_from_slot<kTiles>(p, slots + 8 * (k % kItemSlots)); };
+  auto release_item = [&](int k) {
+    if (kPersist) mbar_arrive(item_empty + 8 * (k % kItemSlots));
+  };
 
   if (warp >= kProducerWarp) {
     if constexpr (L::kSplitRegs) regs_dec<L::kRegsOther>();
-    if (!kPaged && warp == kProducerWarp && lane == 0 && n_max > 0) {
-      // ======================= TMA producer (packed K/V) =======================
-      int issued_k = 0, issued_v = 0;
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(q_full, q_tiles * L::kTile);
-      for (int t = 0; t < q_tiles; ++t)
-#pragma unroll
-        for (int cb = 0; cb < L::kCB; ++cb)
-          tma_load_3d(sQ + t * L::kTile + cb * BM * 128, &tm_q, q_full, cb * 64, h, q0 + m0 + t * BM);
-      for (int j = 0; j < n_max; ++j) {
-        const int sk = j % SK, sv = j % SV;
-        if (!mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag, p.wait_ns)) break;
-        mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
-#pragma unroll
-        for (int cb = 0; cb < L::kCB; ++cb)
-          tma_load_3d(sK + sk * L::kTile + cb * BN * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, k0 + j * BN);
-        ++issued_k;
-        if (!mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag, p.wait_ns)) break;
-        mbar_arrive_expect_tx(v_full + 8 * sv, L::kTile);
-#pragma unroll
-        for (int cb = 0; cb < L::kCB; ++cb)
-          tma_load_3d(sV + sv * L::kTile + cb * BN * 128, &tm_v, v_full + 8 * sv, cb * 64, kvh, k0 + j * BN);
-        ++issued_v;
-      }
-      if (*abort_flag) {
-        // Drain this CTA's own copies before the shared memory goes away.
-        mbar_wait_bounded(q_full, 0, nullptr, nullptr, p.wait_ns);
-        for (int j = max(0, issued_k - SK); j < issued_k; ++j)
-          mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr, p.wait_ns);
-        for (int j = max(0, issued_v - SV); j < issued_v; ++j)
-          mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr, p.wait_ns);
-      }
-    } else if (kPaged && warp == kProducerWarp && n_max > 0) {
-      // ======================= TMA producer (paged K/V) ========================
-      // The whole warp: lane l brings token rows [l' * rows_per_box, ...) of
-      // column block cb (l = l' * kCB + cb) of one K or V tile from its page.
-      const int rpb = p.rows_per_box;
-      const int pages_per_tile = BN / rpb;
-      const int i_page = lane / L::kCB, cb = lane - i_page * L::kCB;
-      int issued_k = 0, issued_v = 0, tails = 0;
+    if (warp == kProducerWarp) {
+      // ============================ TMA producer ============================
+      // The whole warp: it claims and describes the items (persistent grid) and
+      // publishes them to the consumers.  Ring positions and phases run on
+      // across items; an item's Q waits until the previous item's last Q.K^T
+      // has read the Q buffers (q_empty).  Packed K/V: lane 0 issues the copies.
+      // Paged K/V: lane l brings token rows [l' * rows_per_box, ...) of column
+      // block cb (l = l' * kCB + cb) of one K or V tile from its page.
+      [[maybe_unused]] const int rpb = p.rows_per_box;
+      [[maybe_unused]] const int pages_per_tile = kPaged ? BN / rpb : 0;
+      [[maybe_unused]] const int i_page = lane / L::kCB, cb = lane - i_page * L::kCB;
+      int issued_k = 0, issued_v = 0, tails = 0, loads_q = 0;
       if (lane == 0) {
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
-        mbar_arrive_expect_tx(q_full, q_tiles * L::kTile);
-        for (int t = 0; t < q_tiles; ++t)
-#pragma unroll
-          for (int c2 = 0; c2 < L::kCB; ++c2)
-            tma_load_3d(sQ + t * L::kTile + c2 * BM * 128, &tm_q, q_full, c2 * 64, h, q0 + m0 + t * BM);
+      }
+      ItemCursor cur{p.num_pairs, 0, 0, 0, 0};
+      int claimed = 0;  // lane 0: the rank claimed for the next item
+      if (kPersist) {
+        if (kPaged && blockIdx.x == 0)
+          for (int b = lane; b < p.batch; b += 32)
+            if (__ldg(p.seq_lens_k + b) > p.cap_tokens) raise_error(p.err, FAT_DEVERR_BAD_LENGTH);
+        if (lane == 0) claimed = atomicAdd(p.sched, 1);
       }
       bool ok = true;
-      for (int j = 0; ok && j < n_max; ++j) {
-        const int sk = j % SK, sv = j % SV;
-        const int tok0 = j * BN;
-        const int valid_rows = min(BN, kv_len - tok0);
-        // This lane's page: rows [tok0 + i_page * rpb, + rpb) of the sequence.
-        const int row0 = i_page * rpb;
-        int page = -1, slot0 = 0;
-        if (i_page < pages_per_tile && row0 < valid_rows) {
-          const int tok = tok0 + row0;
-          const int lp = tok / p.page_size;
-          slot0 = tok - lp * p.page_size;
-          if (lp < p.max_pages) page = __ldg(p.page_table + (long long)b * p.pt_sb + lp);
-          if (page < 0 || page >= p.num_pages) {
-            raise_error(p.err, FAT_DEVERR_BAD_PAGE);
-            page = -1;
-          }
-        }
-        const unsigned loaded = __ballot_sync(0xffffffffu, page >= 0 && cb == 0);
-        const uint32_t bytes = uint32_t(__popc(loaded)) * uint32_t(rpb) * 128u * L::kCB;
-        // Rows no copy fills (past the sequence, or on a rejected page) are
-        // zeroed in V so that p = 0 there contributes exactly nothing.
-        const bool tail = valid_rows < BN || __popc(loaded) * rpb < BN;
-        // K tile j.
-        if (lane == 0) ok = mbar_wait_bounded(k_empty + 8 * sk, ((j / SK) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane == 0) mbar_arrive_expect_tx(k_full + 8 * sk, bytes);
-        __syncwarp();
-        if (page >= 0)
-          tma_load_4d(sK + sk * L::kTile + cb * BN * 128 + row0 * 128, &tm_k, k_full + 8 * sk, cb * 64, kvh, slot0,
-                      page);
-        ++issued_k;
-        // V tile j.
-        if (lane == 0) ok = mbar_wait_bounded(v_empty + 8 * sv, ((j / SV) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        const uint32_t vbar = tail ? vtail : v_full + 8 * sv;
-        if (lane == 0) mbar_arrive_expect_tx(vbar, bytes);
-        __syncwarp();
-        if (page >= 0)
-          tma_load_4d(sV + sv * L::kTile + cb * BN * 128 + row0 * 128, &tm_v, vbar, cb * 64, kvh, slot0, page);
-        ++issued_v;
-        if (tail) {
-          ++tails;
-          if (lane == 0) ok = mbar_wait_bounded(vtail, (tails - 1) & 1, p.err, abort_flag, p.wait_ns);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-          // Zero every row no copy filled or that lies past the sequence end
-          // (16-byte stores; the swizzle does not matter for zeros), then
-          // publish the tile to the async proxy.
-          const uint32_t vt = sV + sv * L::kTile;
-          for (int i = lane; i < L::kCB * BN * 8; i += 32) {
-            const int c2 = i / (BN * 8), r = (i / 8) % BN;
-            const bool filled = ((loaded >> ((r / rpb) * L::kCB)) & 1u) != 0;
-            if (!filled || r >= valid_rows) {
-              const uint32_t a = vt + uint32_t(c2 * BN * 128 + r * 128 + (i % 8) * 16);
-              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+      for (int k = 0; ok && (kPersist || k < 1); ++k) {
+        Work w{};
+        bool have;
+        if (!kPersist) {
+          have = k == 0;
+          if (have) w = work_from_slot<kTiles>(p, slots);
+        } else {
+          const long long r = __shfl_sync(0xffffffffu, claimed, 0);
+          int b = 0, h = 0, pair = 0;
+          have = cursor_map<kTiles>(p, cur, r, lane, b, h, pair);
+          // Claim the next rank now: its round trip overlaps this item's copies.
+          if (have && lane == 0) claimed = atomicAdd(p.sched, 1);
+          if (have) w = describe_work<kTiles, kPaged>(p, b, h, pair);
+          if (lane == 0) {
+            const int e = k % kItemSlots;
+            ok = mbar_wait_bounded(item_empty + 8 * e, ((k / kItemSlots) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
+            if (ok) {
+              write_slot(slots + 8 * e, w, pair, have);
+              mbar_arrive(item_full + 8 * e);
             }
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(v_full + 8 * sv);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
+        if (!have || !ok) break;
+        if (w.n_max == 0) continue;
+        if (lane == 0) {
+          if (loads_q > 0) ok = mbar_wait_bounded(q_empty, (loads_q - 1) & 1, p.err, abort_flag, p.wait_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(q_full, w.q_tiles * L::kTile);
+            for (int t = 0; t < w.q_tiles; ++t)
+#pragma unroll
+              for (int c2 = 0; c2 < L::kCB; ++c2)
+                tma_load_3d(sQ + t * L::kTile + c2 * BM * 128, &tm_q, q_full, c2 * 64, w.h, w.q0 + w.m0 + t * BM);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ++loads_q;
+        if constexpr (!kPaged) {
+          if (lane == 0) {
+            for (int j = 0; j < w.n_max; ++j) {
+              const int sk = issued_k % SK, sv = issued_v % SV;
+              if (!mbar_wait_bounded(k_empty + 8 * sk, ((issued_k / SK) & 1) ^ 1, p.err, abort_flag, p.wait_ns)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(k_full + 8 * sk, L::kTile);
+#pragma unroll
+              for (int c2 = 0; c2 < L::kCB; ++c2)
+                tma_load_3d(sK + sk * L::kTile + c2 * BN * 128, &tm_k, k_full + 8 * sk, c2 * 64, w.kvh, w.k0 + j * BN);
+              ++issued_k;
+              if (!mbar_wait_bounded(v_empty + 8 * sv, ((issued_v / SV) & 1) ^ 1, p.err, abort_flag, p.wait_ns)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(v_full + 8 * sv, L::kTile);
+#pragma unroll
+              for (int c2 = 0; c2 < L::kCB; ++c2)
+                tma_load_3d(sV + sv * L::kTile + c2 * BN * 128, &tm_v, v_full + 8 * sv, c2 * 64, w.kvh, w.k0 + j * BN);
+              ++issued_v;
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+        } else {
+          const int kv_len = w.kv_len;
+          for (int j = 0; j < w.n_max; ++j) {
+            const int sk = issued_k % SK, sv = issued_v % SV;
+            const int tok0 = j * BN;
+            const int valid_rows = min(BN, kv_len - tok0);
+            // This lane's page: rows [tok0 + i_page * rpb, + rpb) of the sequence.
+            const int row0 = i_page * rpb;
+            int page = -1, slot0 = 0;
+            if (i_page < pages_per_tile && row0 < valid_rows) {
+              const int tok = tok0 + row0;
+              const int lp = tok / p.page_size;
+              slot0 = tok - lp * p.page_size;
+              if (lp < p.max_pages) page = __ldg(p.page_table + (long long)w.b * p.pt_sb + lp);
+              if (page < 0 || page >= p.num_pages) {
+                raise_error(p.err, FAT_DEVERR_BAD_PAGE);
+                page = -1;
+              }
+            }
+            const unsigned loaded = __ballot_sync(0xffffffffu, page >= 0 && cb == 0);
+            const uint32_t bytes = uint32_t(__popc(loaded)) * uint32_t(rpb) * 128u * L::kCB;
+            // Rows no copy fills (past the sequence, or on a rejected page) are
+            // zeroed in V so that p = 0 there contributes exactly nothing.
+            const bool tail = valid_rows < BN || __popc(loaded) * rpb < BN;
+            // K tile j.
+            if (lane == 0)
+              ok = mbar_wait_bounded(k_empty + 8 * sk, ((issued_k / SK) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            if (lane == 0) mbar_arrive_expect_tx(k_full + 8 * sk, bytes);
+            __syncwarp();
+            if (page >= 0)
+              tma_load_4d(sK + sk * L::kTile + cb * BN * 128 + row0 * 128, &tm_k, k_full + 8 * sk, cb * 64, w.kvh,
+                          slot0, page);
+            ++issued_k;
+            // V tile j.
+            if (lane == 0)
+              ok = mbar_wait_bounded(v_empty + 8 * sv, ((issued_v / SV) & 1) ^ 1, p.err, abort_flag, p.wait_ns);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const uint32_t vbar = tail ? vtail : v_full + 8 * sv;
+            if (lane == 0) mbar_arrive_expect_tx(vbar, bytes);
+            __syncwarp();
+            if (page >= 0)
+              tma_load_4d(sV + sv * L::kTile + cb * BN * 128 + row0 * 128, &tm_v, vbar, cb * 64, w.kvh, slot0, page);
+            ++issued_v;
+            if (tail) {
+              ++tails;
+              if (lane == 0) ok = mbar_wait_bounded(vtail, (tails - 1) & 1, p.err, abort_flag, p.wait_ns);
+              ok = __shfl_sync(0xffffffffu, ok, 0);
+              if (!ok) break;
+              // Zero every row no copy filled or that lies past the sequence end
+              // (16-byte stores; the swizzle does not matter for zeros), then
+              // publish the tile to the async proxy.
+              const uint32_t vt = sV + sv * L::kTile;
+              for (int i = lane; i < L::kCB * BN * 8; i += 32) {
+                const int c2 = i / (BN * 8), r = (i / 8) % BN;
+                const bool filled = ((loaded >> ((r / rpb) * L::kCB)) & 1u) != 0;
+                if (!filled || r >= valid_rows) {
+                  const uint32_t a = vt + uint32_t(c2 * BN * 128 + r * 128 + (i % 8) * 16);
+                  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+                }
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(v_full + 8 * sv);
+            }
+          }
         }
       }
       if (*abort_flag && lane == 0) {
-        mbar_wait_bounded(q_full, 0, nullptr, nullptr, p.wait_ns);
+        // Drain this CTA's own copies before the shared memory goes away.
+        if (loads_q > 0) mbar_wait_bounded(q_full, (loads_q - 1) & 1, nullptr, nullptr, p.wait_ns);
         for (int j = max(0, issued_k - SK); j < issued_k; ++j)
           mbar_wait_bounded(k_full + 8 * (j % SK), (j / SK) & 1, nullptr, nullptr, p.wait_ns);
         for (int j = max(0, issued_v - SV); j < issued_v; ++j)
           mbar_wait_bounded(v_full + 8 * (j % SV), (j / SV) & 1, nullptr, nullptr, p.wait_ns);
         if (tails > 0) mbar_wait_bounded(vtail, (tails - 1) & 1, nullptr, nullptr, p.wait_ns);
       }
-    } else if (warp == kMmaWarp && lane == 0 && n_max > 0) {
+    } else if (warp == kMmaWarp && lane == 0) {
       // ============================ MMA issuer ============================
       // The issue loop is kept lean (the tensor core retires an M128 N128 K16
       // MMA every 64 cycles, so per-MMA address arithmetic shows up directly
@@ -400,62 +591,102 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
           if (split) issue_pv(d_tmem, a_tmem + BN / 2, loV, 1u);
         }
       };
-      int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0;
+      int sk = 0, kph = 0, sv = 0, vph = 0, pph0 = 0, pph1 = 0, items_q = 0;
+      // ack_t: tile t's softmax has yet to confirm it saw its previous item's
+      // final phase (its p_full arrival); S_t of the next item waits for it, so
+      // no s_full phase of tile t completes unobserved.
+      bool ack0 = false, ack1 = false;
       // Failure-path test: a wait that nothing ends runs out after p.wait_ns and
       // raises the abort flag; the other roles stop at their next wait.
       if (p.expire) mbar_wait_bounded(never, 0, p.err, abort_flag, p.wait_ns);
-      bool ok = mbar_wait_bounded(q_full, 0, p.err, abort_flag, p.wait_ns);
-      for (int j = 0; ok && j <= n_max; ++j) {
-        if (j < n_max && !mbar_wait_bounded(k_full + 8 * sk, kph, p.err, abort_flag, p.wait_ns)) break;
-        const uint32_t loK = loK0 + uint32_t(sk) * kTileDesc;
-        const uint32_t loV = loV0 + uint32_t(sv) * kTileDesc;
-        bool v_ready = false;
-        // ---- tile 0: O0 += P0 V_{j-1}, then S0 = Q0 K_j^T ----
-        if (j >= 1 && j <= n0) {
-          if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag, p.wait_ns) ||
-              !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag, p.wait_ns))
+      bool ok = true;
+      for (int it = 0; ok && (kPersist || it < 1); ++it) {
+        Work w;
+        if (!consumer_item(it, w, ok)) break;
+        release_item(it);  // read: the slot is free again as far as the issuer goes
+        const int n0 = w.n0, n1 = w.n1, n_max = w.n_max;
+        if (n_max == 0) continue;
+        if (!mbar_wait_bounded(q_full, items_q & 1, p.err, abort_flag, p.wait_ns)) break;
+        ++items_q;
+        for (int j = 0; j <= n_max; ++j) {
+          if (j < n_max && !mbar_wait_bounded(k_full + 8 * sk, kph, p.err, abort_flag, p.wait_ns)) {
+            ok = false;
             break;
-          pph0 ^= 1;
-          v_ready = true;
-          tc::fence_after_sync();
-          issue_p(tmem + L::kColO, tmem + L::kColS, loV, j - 1, 0);
-        }
-        if (j < n0) {
-          tc::fence_after_sync();
-          issue_s(tmem + L::kColS, loQ0, loK);
-        }
-        // One s_full phase per S0 and one more after the last P.V: the softmax
-        // warps then know O0 is final.
-        if (j <= n0 && (j < n0 || j > 0)) tc::commit(s_full);
-        // ---- tile 1 ----
-        if (j >= 1 && j <= n1) {
-          if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag, p.wait_ns) ||
-              (!v_ready && !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag, p.wait_ns)))
-            break;
-          pph1 ^= 1;
-          tc::fence_after_sync();
-          issue_p(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j - 1, 1);
-        }
-        if (j < n1) {
-          tc::fence_after_sync();
-          issue_s(tmem + L::kColS + 128, loQ0 + kTileDesc, loK);
-        }
-        if (j <= n1 && (j < n1 || j > 0)) tc::commit(s_full + 8);
-        // ---- release the tiles this iteration consumed ----
-        if (j >= 1) {  // V_{j-1}
-          tc::commit(v_empty + 8 * sv);
-          if (++sv == SV) {
-            sv = 0;
-            vph ^= 1;
+          }
+          const uint32_t loK = loK0 + uint32_t(sk) * kTileDesc;
+          const uint32_t loV = loV0 + uint32_t(sv) * kTileDesc;
+          bool v_ready = false;
+          // ---- tile 0: O0 += P0 V_{j-1}, then S0 = Q0 K_j^T ----
+          if (j >= 1 && j <= n0) {
+            if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag, p.wait_ns) ||
+                !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag, p.wait_ns)) {
+              ok = false;
+              break;
+            }
+            pph0 ^= 1;
+            v_ready = true;
+            tc::fence_after_sync();
+            issue_p(tmem + L::kColO, tmem + L::kColS, loV, j - 1, 0);
+          }
+          if (j < n0) {
+            if (j == 0 && ack0) {
+              if (!mbar_wait_bounded(p_full, pph0, p.err, abort_flag, p.wait_ns)) {
+                ok = false;
+                break;
+              }
+              pph0 ^= 1;
+              ack0 = false;
+            }
+            tc::fence_after_sync();
+            issue_s(tmem + L::kColS, loQ0, loK);
+          }
+          // One s_full phase per S0 and one more after the last P.V: the softmax
+          // warps then know O0 is final.
+          if (j <= n0 && (j < n0 || j > 0)) tc::commit(s_full);
+          // ---- tile 1 ----
+          if (j >= 1 && j <= n1) {
+            if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag, p.wait_ns) ||
+                (!v_ready && !mbar_wait_bounded(v_full + 8 * sv, vph, p.err, abort_flag, p.wait_ns))) {
+              ok = false;
+              break;
+            }
+            pph1 ^= 1;
+            tc::fence_after_sync();
+            issue_p(tmem + L::kColO + 128, tmem + L::kColS + 128, loV, j - 1, 1);
+          }
+          if (j < n1) {
+            if (j == 0 && ack1) {
+              if (!mbar_wait_bounded(p_full + 8, pph1, p.err, abort_flag, p.wait_ns)) {
+                ok = false;
+                break;
+              }
+              pph1 ^= 1;
+              ack1 = false;
+            }
+            tc::fence_after_sync();
+            issue_s(tmem + L::kColS + 128, loQ0 + kTileDesc, loK);
+          }
+          if (j <= n1 && (j < n1 || j > 0)) tc::commit(s_full + 8);
+          // The item's Q buffers are free once its last Q.K^T completes.
+          if (j == n_max - 1) tc::commit(q_empty);
+          // ---- release the tiles this iteration consumed ----
+          if (j >= 1) {  // V_{j-1}
+            tc::commit(v_empty + 8 * sv);
+            if (++sv == SV) {
+              sv = 0;
+              vph ^= 1;
+            }
+          }
+          if (j < n_max) {  // K_j
+            tc::commit(k_empty + 8 * sk);
+            if (++sk == SK) {
+              sk = 0;
+              kph ^= 1;
+            }
           }
         }
-        if (j < n_max) {  // K_j
-          tc::commit(k_empty + 8 * sk);
-          if (++sk == SK) {
-            sk = 0;
-            kph ^= 1;
-          }
-        }
+        ack0 = ack0 || n0 > 0;
+        ack1 = ack1 || n1 > 0;
       }
       // Every MMA this thread issued has finished once `drain` completes.
       tc::commit(drain);
@@ -466,106 +697,83 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     // ============================ softmax warpgroups ============================
     const int t = warp >> 2;              // query tile of this warpgroup
     const int row = tid & 127;            // row of the tile = tensor-memory lane
-    const int n_t = t == 0 ? n0 : n1;
     const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
     const uint32_t colS = L::kColS + 128 * t, colO = L::kColO + 128 * t;
     const uint32_t sbar = s_full + 8 * t, pbar = p_full + 8 * t;
-    const int q_idx = m0 + t * BM + row;
-    // Last key this row may see (inclusive).
-    const int lim = p.causal ? min(kv_len - 1, q_idx + offset) : kv_len - 1;
-    float m_used = -CUDART_INF_F, l_sum = 0.f;
+    uint32_t sph = 0;  // parity of the next s_full phase of this tile (runs on across items)
     bool ok = true;
-    for (int j = 0; j < n_t; ++j) {
-      if (!mbar_wait_bounded(sbar, j & 1, p.err, abort_flag, p.wait_ns)) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      float s[BN];
+    for (int it = 0; ok && (kPersist || it < 1); ++it) {
+      int n_t, lim;  // K/V tiles of this tile; last key this row may see (inclusive)
       {
-        uint32_t r[BN / 32][32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + colS + 32 * c, r[c]);
-        tc::wait_ld();
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[c][i]);
+        Work w;
+        if (!consumer_item(it, w, ok)) break;
+        n_t = t == 0 ? w.n0 : w.n1;
+        const int q_idx = w.m0 + t * BM + row;
+        lim = p.causal ? min(w.kv_len - 1, q_idx + w.offset) : w.kv_len - 1;
       }
-      const int kv0 = j * BN;
-      if (kv0 + BN - 1 > lim) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) s[i] = (kv0 + i <= lim) ? s[i] : -CUDART_INF_F;
-      }
-      float mx;
-      {
-        // Four independent chains over the BN scores: blocks of 8 from 0.
-        static_assert(BN % 8 == 0, "row max works on blocks of 8 scores");
-        float a0 = fmaxf(s[0], s[4]), a1 = fmaxf(s[1], s[5]), a2 = fmaxf(s[2], s[6]), a3 = fmaxf(s[3], s[7]);
-#pragma unroll
-        for (int i = 8; i < BN; i += 8) {
-          a0 = max3(a0, s[i], s[i + 4]);
-          a1 = max3(a1, s[i + 1], s[i + 5]);
-          a2 = max3(a2, s[i + 2], s[i + 6]);
-          a3 = max3(a3, s[i + 3], s[i + 7]);
+      float m_used = -CUDART_INF_F, l_sum = 0.f;
+      for (int j = 0; j < n_t; ++j) {
+        if (!mbar_wait_bounded(sbar, sph, p.err, abort_flag, p.wait_ns)) {
+          ok = false;
+          break;
         }
-        mx = fmaxf(max3(a0, a1, a2), a3);
-      }
-      mx *= p.scale_log2;
-      float factor = 1.f;
-      bool grow = false;
-      if (mx > m_used + kRescaleThreshold) {
-        factor = (m_used == -CUDART_INF_F) ? 1.f : fast_exp2(m_used - mx);
-        grow = m_used != -CUDART_INF_F;
-        m_used = mx;
-        l_sum *= factor;
-      }
-      if (__any_sync(0xffffffffu, grow)) {
-        // S_t(j) is complete, so O_t holds every earlier P.V: rescale in place.
+        sph ^= 1;
+        tc::fence_after_sync();
+        float s[BN];
+        {
+          uint32_t r[BN / 32][32];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tc::ld32(lane_base + colO + 32 * c, r);
+          for (int c = 0; c < BN / 32; ++c) tc::ld32(lane_base + colS + 32 * c, r[c]);
           tc::wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          tc::st32(lane_base + colO + 32 * c, r);
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[c][i]);
         }
-      }
-      const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-      if constexpr (!kSplit) {
-        // P rounded to the input dtype (prefill.py:128), packed over S's first 64 columns.
+        const int kv0 = j * BN;
+        if (kv0 + BN - 1 > lim) {
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t packed[32];
+          for (int i = 0; i < BN; ++i) s[i] = (kv0 + i <= lim) ? s[i] : -CUDART_INF_F;
+        }
+        float mx;
+        {
+          // Four independent chains over the BN scores: blocks of 8 from 0.
+          static_assert(BN % 8 == 0, "row max works on blocks of 8 scores");
+          float a0 = fmaxf(s[0], s[4]), a1 = fmaxf(s[1], s[5]), a2 = fmaxf(s[2], s[6]), a3 = fmaxf(s[3], s[7]);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float x0, x1, x2, x3;
-            fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
-            fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
-            const float p0 = fast_exp2(x0);
-            const float p1 = fast_exp2(x1);
-            const float p2 = fast_exp2(x2);
-            const float p3 = fast_exp2(x3);
-            add2(sum0, sum1, p0, p1);
-            add2(sum2, sum3, p2, p3);
-            packed[i] = pack2<T>(p0, p1);
-            packed[i + 1] = pack2<T>(p2, p3);
+          for (int i = 8; i < BN; i += 8) {
+            a0 = max3(a0, s[i], s[i + 4]);
+            a1 = max3(a1, s[i + 1], s[i + 5]);
+            a2 = max3(a2, s[i + 2], s[i + 6]);
+            a3 = max3(a3, s[i + 3], s[i + 7]);
           }
-          tc::st32(lane_base + colS + 32 * c, packed);
+          mx = fmaxf(max3(a0, a1, a2), a3);
         }
-        l_sum += (sum0 + sum1) + (sum2 + sum3);
-      } else {
-        // Decided before the exponentials: the row's sum after this tile is at
-        // least its sum so far plus the tile's largest p, so a key of an unsplit
-        // tile still ends with weight <= kSplitTheta.
-        bool split = p.p_split == 2;
-        if (p.p_split == 1) {
-          const float pmax = fast_exp2(mx - msub);
-          split = __any_sync(0xffffffffu, pmax > kSplitTheta * (l_sum + pmax));
+        mx *= p.scale_log2;
+        float factor = 1.f;
+        bool grow = false;
+        if (mx > m_used + kRescaleThreshold) {
+          factor = (m_used == -CUDART_INF_F) ? 1.f : fast_exp2(m_used - mx);
+          grow = m_used != -CUDART_INF_F;
+          m_used = mx;
+          l_sum *= factor;
         }
-        if (!split) {
+        if (__any_sync(0xffffffffu, grow)) {
+          // S_t(j) is complete, so O_t holds every earlier P.V: rescale in place.
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tc::ld32(lane_base + colO + 32 * c, r);
+            tc::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+            tc::st32(lane_base + colO + 32 * c, r);
+          }
+        }
+        const float msub = (m_used == -CUDART_INF_F) ? 0.f : m_used;
+        float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+        if constexpr (!kSplit) {
+          // P rounded to the input dtype (prefill.py:128), packed over S's first 64 columns.
 #pragma unroll
           for (int c = 0; c < BN / 64; ++c) {
             uint32_t packed[32];
@@ -585,131 +793,182 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
             }
             tc::st32(lane_base + colS + 32 * c, packed);
           }
-          if (p.p_split == 1) {
-            // Another warp of this tile may vote to split: the remainder pass then
-            // reads these rows' columns [64, 128), which must hold zeros.
-            uint32_t zero[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) zero[i] = 0u;
-            tc::st32(lane_base + colS + BN / 2, zero);
-            tc::st32(lane_base + colS + BN / 2 + 32, zero);
-          }
+          l_sum += (sum0 + sum1) + (sum2 + sum3);
         } else {
-          // Head in columns [0, 64), remainder p - head in [64, 128): every score
-          // of this S row is already in registers, so those columns are free.
+          // Decided before the exponentials: the row's sum after this tile is at
+          // least its sum so far plus the tile's largest p, so a key of an unsplit
+          // tile still ends with weight <= kSplitTheta.
+          bool split = p.p_split == 2;
+          if (p.p_split == 1) {
+            const float pmax = fast_exp2(mx - msub);
+            split = __any_sync(0xffffffffu, pmax > kSplitTheta * (l_sum + pmax));
+          }
+          if (!split) {
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t hi[16], lo[16];
+            for (int c = 0; c < BN / 64; ++c) {
+              uint32_t packed[32];
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              float x0, x1, x2, x3;
-              fma2(x0, x1, s[32 * c + 2 * i], s[32 * c + 2 * i + 1], p.scale_log2, -msub);
-              fma2(x2, x3, s[32 * c + 2 * i + 2], s[32 * c + 2 * i + 3], p.scale_log2, -msub);
-              const float p0 = fast_exp2(x0);
-              const float p1 = fast_exp2(x1);
-              const float p2 = fast_exp2(x2);
-              const float p3 = fast_exp2(x3);
-              add2(sum0, sum1, p0, p1);
-              add2(sum2, sum3, p2, p3);
-              split_hi_lo<T>(p0, p1, hi[i], lo[i]);
-              split_hi_lo<T>(p2, p3, hi[i + 1], lo[i + 1]);
+              for (int i = 0; i < 32; i += 2) {
+                float x0, x1, x2, x3;
+                fma2(x0, x1, s[64 * c + 2 * i], s[64 * c + 2 * i + 1], p.scale_log2, -msub);
+                fma2(x2, x3, s[64 * c + 2 * i + 2], s[64 * c + 2 * i + 3], p.scale_log2, -msub);
+                const float p0 = fast_exp2(x0);
+                const float p1 = fast_exp2(x1);
+                const float p2 = fast_exp2(x2);
+                const float p3 = fast_exp2(x3);
+                add2(sum0, sum1, p0, p1);
+                add2(sum2, sum3, p2, p3);
+                packed[i] = pack2<T>(p0, p1);
+                packed[i + 1] = pack2<T>(p2, p3);
+              }
+              tc::st32(lane_base + colS + 32 * c, packed);
             }
-            tc::st16(lane_base + colS + 16 * c, hi);
-            tc::st16(lane_base + colS + BN / 2 + 16 * c, lo);
+            if (p.p_split == 1) {
+              // Another warp of this tile may vote to split: the remainder pass then
+              // reads these rows' columns [64, 128), which must hold zeros.
+              uint32_t zero[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) zero[i] = 0u;
+              tc::st32(lane_base + colS + BN / 2, zero);
+              tc::st32(lane_base + colS + BN / 2 + 32, zero);
+            }
+          } else {
+            // Head in columns [0, 64), remainder p - head in [64, 128): every score
+            // of this S row is already in registers, so those columns are free.
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+              uint32_t hi[16], lo[16];
+#pragma unroll
+              for (int i = 0; i < 16; i += 2) {
+                float x0, x1, x2, x3;
+                fma2(x0, x1, s[32 * c + 2 * i], s[32 * c + 2 * i + 1], p.scale_log2, -msub);
+                fma2(x2, x3, s[32 * c + 2 * i + 2], s[32 * c + 2 * i + 3], p.scale_log2, -msub);
+                const float p0 = fast_exp2(x0);
+                const float p1 = fast_exp2(x1);
+                const float p2 = fast_exp2(x2);
+                const float p3 = fast_exp2(x3);
+                add2(sum0, sum1, p0, p1);
+                add2(sum2, sum3, p2, p3);
+                split_hi_lo<T>(p0, p1, hi[i], lo[i]);
+                split_hi_lo<T>(p2, p3, hi[i + 1], lo[i + 1]);
+              }
+              tc::st16(lane_base + colS + 16 * c, hi);
+              tc::st16(lane_base + colS + BN / 2 + 16 * c, lo);
+            }
+          }
+          l_sum += (sum0 + sum1) + (sum2 + sum3);
+          if (p.p_split == 1 && lane == 0) votes[t * 8 + (warp & 3) * 2 + (j & 1)] = split ? 1 : 0;
+        }
+        tc::wait_st();
+        tc::fence_before_sync();
+        mbar_arrive(pbar);
+      }
+      // ---- epilogue: O / l -> global, once the last P.V of this tile completed ----
+      // (the item is described again here, so nothing of it stays live in the loop)
+      const Work w = peek_item(it);
+      const int q0 = w.q0, q_len = w.q_len, m0 = w.m0, h = w.h;
+      // Only a CTA's single item (one CTA per item) may stage O in its Q buffers:
+      // in the persistent grid the producer refills them for the next item.
+      const bool last = !kPersist;
+      const int q_idx = m0 + t * BM + row;
+      bool fin = false;
+      if (ok && n_t > 0) {
+        fin = mbar_wait_bounded(sbar, sph, p.err, abort_flag, p.wait_ns);
+        if (fin) {
+          sph ^= 1;
+          // Seen final: the issuer may now start this tile's next item (S_t only;
+          // O_t is overwritten after this tile's next P arrives).
+          mbar_arrive(pbar);
+        } else {
+          ok = false;
+        }
+      }
+      // A warp whose 32 rows all belong to the sequence stages them, 16-bit and
+      // 128-byte swizzled, in its rows of the tile's Q buffer (unused once the
+      // tile's last MMA completed) and stores them with one TMA copy per 64
+      // columns: whole 128-byte lines leave instead of each store instruction
+      // touching 32 rows' lines with 16 bytes.  Rows of a partial group (the
+      // next sequence's rows follow in out) take the direct stores below.
+      const int wrow0 = m0 + t * BM + 32 * (warp & 3);
+      if (p.o_tma && last && n_t > 0 && wrow0 + 32 <= q_len) {
+        if (__all_sync(0xffffffffu, fin)) {
+          tc::fence_after_sync();
+          const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+          const uint32_t qt = sQ + uint32_t(t * L::kTile);
+#pragma unroll
+          for (int c = 0; c < D / 32; c += 2) {
+            uint32_t r[2][32];
+            tc::ld32(lane_base + colO + 32 * c, r[0]);
+            tc::ld32(lane_base + colO + 32 * (c + 1), r[1]);
+            tc::wait_ld();
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const uint32_t blk = qt + uint32_t(((c + u) >> 1) * BM * 128);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t* x = r[u] + 8 * i;
+                st_shared_v4(blk + swz128(uint32_t(row), uint32_t(((c + u) & 1) * 4 + i)),
+                             pack2<T>(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
+                             pack2<T>(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
+                             pack2<T>(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
+                             pack2<T>(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+#pragma unroll
+            for (int cb = 0; cb < L::kCB; ++cb)
+              tma_store_3d(&tm_o, qt + uint32_t(cb * BM * 128 + (warp & 3) * 32 * 128), cb * 64, h, q0 + wrow0);
+            bulk_commit_group();
+            bulk_wait_read_all();
           }
         }
-        l_sum += (sum0 + sum1) + (sum2 + sum3);
-        if (p.p_split == 1 && lane == 0) votes[t * 8 + (warp & 3) * 2 + (j & 1)] = split ? 1 : 0;
-      }
-      tc::wait_st();
-      tc::fence_before_sync();
-      mbar_arrive(pbar);
-    }
-    // ---- epilogue: O / l -> global, once the last P.V of this tile completed ----
-    const bool fin = ok && n_t > 0 && mbar_wait_bounded(sbar, n_t & 1, p.err, abort_flag, p.wait_ns);
-    // A warp whose 32 rows all belong to the sequence stages them, 16-bit and
-    // 128-byte swizzled, in its rows of the tile's Q buffer (unused once the
-    // tile's last MMA completed) and stores them with one TMA copy per 64
-    // columns: whole 128-byte lines leave instead of each store instruction
-    // touching 32 rows' lines with 16 bytes.  Rows of a partial group (the
-    // next sequence's rows follow in out) take the direct stores below.
-    const int wrow0 = m0 + t * BM + 32 * (warp & 3);
-    if (p.o_tma && n_t > 0 && wrow0 + 32 <= q_len) {
-      if (__all_sync(0xffffffffu, fin)) {
+      } else if (fin) {
         tc::fence_after_sync();
         const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-        const uint32_t qt = sQ + uint32_t(t * L::kTile);
+        const bool store = q_idx < q_len;
+        const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
 #pragma unroll
-        for (int c = 0; c < D / 32; c += 2) {
-          uint32_t r[2][32];
-          tc::ld32(lane_base + colO + 32 * c, r[0]);
-          tc::ld32(lane_base + colO + 32 * (c + 1), r[1]);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::ld32(lane_base + colO + 32 * c, r);
           tc::wait_ld();
+          if (store) {
+            if (p.out_f32) {
+              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + 32 * c);
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const uint32_t blk = qt + uint32_t(((c + u) >> 1) * BM * 128);
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
+                                     __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + base + 32 * c);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint32_t* x = r[u] + 8 * i;
-              st_shared_v4(blk + swz128(uint32_t(row), uint32_t(((c + u) & 1) * 4 + i)),
-                           pack2<T>(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
-                           pack2<T>(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
-                           pack2<T>(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
-                           pack2<T>(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+              for (int i = 0; i < 4; ++i) {
+                uint4 v;
+                v.x = pack2<T>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+                v.y = pack2<T>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+                v.z = pack2<T>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+                v.w = pack2<T>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+                dst[i] = v;
+              }
             }
           }
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-#pragma unroll
-          for (int cb = 0; cb < L::kCB; ++cb)
-            tma_store_3d(&tm_o, qt + uint32_t(cb * BM * 128 + (warp & 3) * 32 * 128), cb * 64, h, q0 + wrow0);
-          bulk_commit_group();
-          bulk_wait_read_all();
-        }
-      }
-    } else if (fin) {
-      tc::fence_after_sync();
-      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      const bool store = q_idx < q_len;
-      const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tc::ld32(lane_base + colO + 32 * c, r);
-        tc::wait_ld();
-        if (store) {
+      } else if (n_t == 0 && q_idx < q_len) {
+        // No visible keys (only reachable with invalid causal inputs): zeros.
+        const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
+        for (int d = 0; d < D; ++d) {
           if (p.out_f32) {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + 32 * c);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
-                                   __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
+            reinterpret_cast<float*>(p.out)[base + d] = 0.f;
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + base + 32 * c);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = pack2<T>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
-              v.y = pack2<T>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
-              v.z = pack2<T>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
-              v.w = pack2<T>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
-              dst[i] = v;
-            }
+            reinterpret_cast<T*>(p.out)[base + d] = from_float<T>(0.f);
           }
         }
       }
-    } else if (n_t == 0 && q_idx < q_len) {
-      // No visible keys (only reachable with invalid causal inputs): zeros.
-      const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
-      for (int d = 0; d < D; ++d) {
-        if (p.out_f32) {
-          reinterpret_cast<float*>(p.out)[base + d] = 0.f;
-        } else {
-          reinterpret_cast<T*>(p.out)[base + d] = from_float<T>(0.f);
-        }
-      }
+      __syncwarp();
+      if (lane == 0) release_item(it);
     }
   }
 
@@ -717,6 +976,14 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == kMmaWarp) tc::tmem_dealloc(tmem, kTmemCols);
+  if (kPersist && tid == 0) {
+    // The last CTA to finish zeroes the counters for the next launch on this stream.
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == int(gridDim.x) - 1) {
+      atomicExch(p.sched, 0);
+      atomicExch(p.sched + 1, 0);
+    }
+  }
 }
 
 }  // namespace pre
@@ -725,6 +992,65 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
 // Host side
 // =============================================================================
 namespace {
+
+// Work counters of the persistent grid, one pair {next rank, CTAs done} per
+// (device, stream).  Launches on one stream run in order and the last CTA of
+// each launch zeroes its pair, so every launch finds it zero.  Made on a
+// stream's first prefill outside stream capture (a cudaMalloc, then a
+// cudaMemsetAsync on that stream); a stream first seen while it is being
+// captured gets none, and its launches use one CTA per item.  Never freed
+// (8 bytes per stream).
+int* prefill_counters(int device, cudaStream_t stream) {
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, int*> counters;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(device, reinterpret_cast<uintptr_t>(stream));
+  const auto it = counters.find(key);
+  if (it != counters.end()) return it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  int* c = nullptr;
+  if (cudaMalloc(&c, 2 * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaMemsetAsync(c, 0, 2 * sizeof(int), stream) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(c);
+    return nullptr;
+  }
+  counters[key] = c;
+  return c;
+}
+
+// Grid of a prefill launch.  Persistent (the default for rounded P): one CTA
+// per SM, each claiming items from the stream's counters until none is left,
+// so an item's Q and first K/V copies and its first Q.K^T overlap the previous
+// item's last softmax and output stores, tensor memory and barriers are set up
+// once per SM, and SMs that finish early take more items.  Otherwise one CTA
+// per (head, sequence, pair), heaviest pairs first.  Returns the kernel.
+using PrefillKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                               const pre::Params);
+
+template <typename T, int D, bool kPaged>
+PrefillKernel plan_prefill(const PrefillArgs& a, int p_split, pre::Params& p, dim3* grid) {
+  using L = pre::Layout<D>;
+  const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
+  p.batch = a.batch;
+  p.num_pairs = pairs;
+  const int device = current_device();
+  const int g = sm_count(device);
+  p.sched = (p_split == 0 && prefill_schedule() == 0 && g > 0) ? prefill_counters(device, a.stream) : nullptr;
+  if (p.sched != nullptr) {
+    *grid = dim3(unsigned(g));
+    return pre::prefill_kernel<T, D, kPaged, false, true>;
+  }
+  *grid = dim3(unsigned(a.num_heads * a.batch), unsigned(pairs));
+  return p_split != 0 ? pre::prefill_kernel<T, D, kPaged, true, false> : pre::prefill_kernel<T, D, kPaged, false, false>;
+}
 
 // Map of the 16-bit output {head_dim, head, token} in 64-column, 32-row boxes
 // (the epilogue's TMA stores).  fp32 output, or a layout the map cannot
@@ -749,7 +1075,9 @@ template <typename T, int D>
 int launch_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
   const int p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
-  auto kern = p_split != 0 ? pre::prefill_kernel<T, D, false, true> : pre::prefill_kernel<T, D, false, false>;
+  pre::Params p{};
+  dim3 grid;
+  const PrefillKernel kern = plan_prefill<T, D, false>(a, p_split, p, &grid);
   static_assert(L::kSmem <= 227 * 1024, "prefill tiles exceed shared memory");
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill)", e);
@@ -774,7 +1102,6 @@ int launch_t(const PrefillArgs& a) {
                       &why))
       return invalid("prefill v: " + why);
   }
-  pre::Params p{};
   CUtensorMap to;
   p.o_tma = encode_out_map<D>(a, tq, &to);
   p.cu_q = a.cu_q;
@@ -791,8 +1118,6 @@ int launch_t(const PrefillArgs& a) {
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
   p.p_split = p_split;
-  const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
-  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill launch", e);
@@ -803,7 +1128,9 @@ template <typename T, int D>
 int launch_paged_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
   const int p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
-  auto kern = p_split != 0 ? pre::prefill_kernel<T, D, true, true> : pre::prefill_kernel<T, D, true, false>;
+  pre::Params p{};
+  dim3 grid;
+  const PrefillKernel kern = plan_prefill<T, D, true>(a, p_split, p, &grid);
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), int(L::kSmem), current_device());
   if (e != cudaSuccess) return cuda_failure("cudaFuncSetAttribute(prefill paged)", e);
   std::string why;
@@ -829,7 +1156,6 @@ int launch_paged_t(const PrefillArgs& a) {
                       &why))
       return invalid("prefill v_cache: " + why);
   }
-  pre::Params p{};
   CUtensorMap to;
   p.o_tma = encode_out_map<D>(a, tq, &to);
   p.cu_q = a.cu_q;
@@ -853,8 +1179,6 @@ int launch_paged_t(const PrefillArgs& a) {
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
   p.p_split = p_split;
-  const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
-  dim3 grid(unsigned(a.num_heads * a.batch), unsigned(pairs));
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill paged launch", e);

@@ -53,6 +53,31 @@ def p_precision(mode: str):
         set_p_precision(prev)
 
 
+SCHEDULES = {"persistent": 0, "per_item": 1}
+
+
+def set_schedule(mode: str) -> str:
+    """Set the prefill grid for later launches; returns the previous one.
+
+    ``"persistent"`` (default: one CTA per SM claiming (head, sequence,
+    256-row query pair) items from a per-stream counter) or ``"per_item"``
+    (one CTA per item).  Outputs are bitwise identical."""
+    if mode not in SCHEDULES:
+        raise ValueError(f"unknown prefill schedule {mode!r}; expected one of {sorted(SCHEDULES)}")
+    prev = _lib.load().fat_set_prefill_schedule(SCHEDULES[mode])
+    return {v: k for k, v in SCHEDULES.items()}[prev]
+
+
+@contextlib.contextmanager
+def schedule(mode: str):
+    """Context manager form of :func:`set_schedule`."""
+    prev = set_schedule(mode)
+    try:
+        yield
+    finally:
+        set_schedule(prev)
+
+
 def _resolve_config(config: dict | None) -> dict:
     """``prefill.py:167-191`` without the persisted tuning lookup."""
     resolved = dict(DEFAULT_CONFIG)

@@ -101,6 +101,20 @@ void fat_expire_next_waits(int launches);
 int fat_set_prefill_p_split(int mode);
 
 /*
+ * Grid of the prefill launches made from now on (process-wide; both prefill
+ * entry points, all dtypes):
+ *    0  persistent (default): one CTA per SM, each claiming (head, sequence,
+ *       256-row query pair) items, heaviest first, from a per-stream counter
+ *       until none is left, so an item's first loads and Q.K^T overlap the
+ *       previous item's last softmax and output stores.  The counter (8 bytes
+ *       of device memory per stream) is made on a stream's first prefill; a
+ *       stream first used while it is being captured into a graph runs mode 1
+ *    1  one CTA per item
+ * Results are bitwise identical.  Returns the previous setting, or -2 (message
+ * in fat_last_error) for another value.  No reference counterpart. */
+int fat_set_prefill_schedule(int mode);
+
+/*
  * Bytes of scratch fat_paged_decode needs for this problem on `device`.
  * The caller zero-fills the buffer once; every successful call leaves it
  * zero-filled again, so one buffer serves any number of calls that are
