@@ -22,8 +22,8 @@ uint64_t fat_set_wait_limit_ns(uint64_t limit_ns) { return fat::set_wait_limit_n
 void fat_expire_next_waits(int launches) { fat::request_expiry(launches); }
 
 int fat_set_prefill_p_split(int mode) {
-  if (mode < -1 || mode > 2) {
-    fat::set_last_error("prefill p_split must be -1, 0, 1 or 2, got " + std::to_string(mode));
+  if (mode < -1 || mode > 3) {
+    fat::set_last_error("prefill p_split must be -1, 0, 1, 2 or 3, got " + std::to_string(mode));
     return -2;
   }
   fat::set_last_error("");

@@ -46,7 +46,7 @@ int set_prefill_p_split(int mode) { return g_p_split.exchange(mode, std::memory_
 
 int prefill_p_split(bool bf16) {
   const int mode = g_p_split.load(std::memory_order_relaxed);
-  return mode >= 0 ? mode : (bf16 ? 1 : 0);
+  return mode >= 0 ? mode : (bf16 ? 3 : 0);
 }
 
 uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }

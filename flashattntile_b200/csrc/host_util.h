@@ -33,9 +33,10 @@ bool take_expire_request();
 void request_expiry(int n);
 
 // How prefill feeds P into P.V (fat_set_prefill_p_split): -1 automatic (bf16:
-// mode 1; fp16: mode 0), 0 rounded once (the reference kernel's arithmetic), 1
-// a 16-bit remainder on key tiles holding a key that weighs more than 1/16 of
-// its row so far, 2 remainder on every key tile.
+// mode 3, paged K/V mode 1; fp16: mode 0), 0 rounded once (the reference
+// kernel's arithmetic), 1 a 16-bit remainder on key tiles holding a key that
+// weighs more than 1/16 of its row so far, 2 remainder on every key tile, 3
+// (bf16) P.V in fp16 against a scaled fp16 copy of V.
 int set_prefill_p_split(int mode);  // returns the previous setting
 int prefill_p_split(bool bf16);     // the mode a launch of that dtype uses
 

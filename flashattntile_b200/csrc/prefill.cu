@@ -80,6 +80,8 @@ struct Params {
   int p_split;           // P into P.V as head + remainder: 0 never, 1 where a key weighs (vote), 2 always
   int batch, num_pairs;  // sequences; 2-tile query pairs of the longest sequence
   int* sched;            // kPersist: {next rank, CTAs done}, zero at launch and zeroed again by the last CTA
+  const unsigned* pv_emax;  // kHalfPV: largest |v| (bf16 bits) per (sequence, KV head), b * Hkv + kv head
+  int num_kv_heads;
 };
 
 // p_split == 1: a key tile of a query tile enters P.V as a 16-bit head plus a
@@ -157,6 +159,16 @@ struct Work {
   int b, h, kvh, q0, q_len, k0, kv_len, m0, offset, n0, n1, n_max, q_tiles;
 };
 
+// kHalfPV: V of (sequence, KV head) was stored as fp16 times 2^-e, e = E - 14
+// for E the binary exponent of its largest |v|: every scaled value is below
+// 2^15 (inside fp16's range) and the largest at least 2^14 (small V keeps
+// fp16's full precision); the output is scaled back by 2^e.  e is kept in
+// [-100, 114] so that 2^e and 2^-e are normal floats (an all-zero V gets -100).
+__host__ __device__ __forceinline__ int pv_exponent(unsigned absmax_bits) {
+  const int biased = int((absmax_bits >> 7) & 0xffu);  // bf16: 8 exponent bits above 7 mantissa bits
+  return min(114, max(-100, biased - 127 - 14));
+}
+
 // The tile counts of an item whose sequence fields are set.
 template <int kTiles>
 __device__ __forceinline__ void finish_work(const Params& p, int pair, Work& w) {
@@ -207,6 +219,16 @@ __device__ __forceinline__ void write_slot(volatile int* d, const Work& w, int p
   d[4] = w.q_len;
   d[5] = w.k0;
   d[6] = w.kv_len;
+}
+
+template <bool kHalfPV>
+__device__ __forceinline__ float pv_unscale(const Params& p, const Work& w) {
+  if constexpr (!kHalfPV) {
+    return 1.f;
+  } else {
+    const int e = pv_exponent(__ldg(p.pv_emax + (long long)w.b * p.num_kv_heads + w.kvh));
+    return __int_as_float((127 + e) << 23);  // 2^e, -100 <= e <= 114
+  }
 }
 
 // Persistent grid: the live items in one global order -- query pair index
@@ -263,12 +285,15 @@ __device__ bool cursor_map(const Params& p, ItemCursor& c, long long r, int lane
 // kPaged: K/V come from a paged cache through the page table (4-D maps
 // {head_dim, kv head, slot, page}); otherwise from packed [tokens, heads, dim].
 // kSplit: this instantiation can feed P as head + remainder (p_split 1 and 2).
+// kHalfPV (bf16 inputs, packed K/V): P.V in fp16 -- P rounded to fp16, V read
+// from an fp16 copy scaled by 2^-e per (sequence, KV head) (pv_emax), and the
+// output multiplied by 2^e.
 // kPersist: one CTA per SM claiming items (rounded P only: the split kernel's
 // softmax and issuer need every register they have, and its per-item build runs
 // faster); otherwise one CTA per item.
 // The other one is the plain kernel, without the split code in its softmax loop
 // (compiled apart: the branch alone cost 13% in the common path).
-template <typename T, int D, bool kPaged, bool kSplit, bool kPersist>
+template <typename T, int D, bool kPaged, bool kSplit, bool kPersist, bool kHalfPV>
 __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -279,7 +304,8 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   constexpr int kProducerWarp = L::kProducerWarp, kMmaWarp = L::kMmaWarp;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdescQK = tc::idesc_f16(BM, BN, fmt, 0, 0);
-  constexpr uint32_t kIdescPV = tc::idesc_f16(BM, D, fmt, 0, 1);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(BM, D, kHalfPV ? 0 : fmt, 0, 1);
+  using PT = std::conditional_t<kHalfPV, __half, T>;  // P's 16-bit type
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -788,8 +814,8 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
               const float p3 = fast_exp2(x3);
               add2(sum0, sum1, p0, p1);
               add2(sum2, sum3, p2, p3);
-              packed[i] = pack2<T>(p0, p1);
-              packed[i + 1] = pack2<T>(p2, p3);
+              packed[i] = pack2<PT>(p0, p1);
+              packed[i + 1] = pack2<PT>(p2, p3);
             }
             tc::st32(lane_base + colS + 32 * c, packed);
           }
@@ -893,7 +919,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
       if (p.o_tma && last && n_t > 0 && wrow0 + 32 <= q_len) {
         if (__all_sync(0xffffffffu, fin)) {
           tc::fence_after_sync();
-          const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+          const float inv = (l_sum > 0.f ? 1.f / l_sum : 0.f) * pv_unscale<kHalfPV>(p, w);
           const uint32_t qt = sQ + uint32_t(t * L::kTile);
 #pragma unroll
           for (int c = 0; c < D / 32; c += 2) {
@@ -927,7 +953,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         }
       } else if (fin) {
         tc::fence_after_sync();
-        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        const float inv = (l_sum > 0.f ? 1.f / l_sum : 0.f) * pv_unscale<kHalfPV>(p, w);
         const bool store = q_idx < q_len;
         const long long base = (long long)(q0 + q_idx) * p.o_st + (long long)h * p.o_sh;
 #pragma unroll
@@ -986,6 +1012,136 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   }
 }
 
+// ---- kHalfPV pre-pass: bf16 V -> fp16 copy scaled per (sequence, KV head) ----
+// Block (x, y): tokens [64 x, 64 x + 64) of KV head y; thread i takes the
+// 16-byte vectors i, i + 256, ... of that 64-row slab (all loads issued first).
+// A slab inside one sequence (the common case) looks its sequence up once.
+constexpr int kVRows = 64;
+constexpr int kVThreads = 256;
+
+// The sequence of packed token t: the largest b with cu[b] <= t.
+__device__ __forceinline__ int seq_of_token(const int* cu, int batch, long long t) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(cu + mid) <= t) {
+      lo = mid;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  return lo;
+}
+
+template <int D>
+struct VSlab {
+  static constexpr int kVecs = D / 8;                          // 16-byte vectors per token row
+  static constexpr int kPerThread = kVRows * kVecs / kVThreads;  // vectors per thread
+  static_assert(kVRows * kVecs % kVThreads == 0, "slab splits evenly");
+};
+
+// The slab's sequence when all its tokens belong to one, else -1.
+__device__ __forceinline__ int slab_sequence(const int* cu_k, int batch, long long t0, long long total_k) {
+  __shared__ int seq;
+  if (threadIdx.x == 0) {
+    const long long t1 = min(t0 + kVRows, total_k) - 1;
+    const int b0 = seq_of_token(cu_k, batch, t0), b1 = seq_of_token(cu_k, batch, t1);
+    seq = b0 == b1 ? b0 : -1;
+  }
+  __syncthreads();
+  return seq;
+}
+
+// Largest |v| per (sequence, KV head) as bf16 bits without the sign (a bf16
+// magnitude orders like its bit pattern; NaN compares above inf), into emax
+// (zeroed before): one atomic per slab (per token in a slab that straddles
+// sequences).
+template <int D>
+__global__ void __launch_bounds__(kVThreads) v_absmax_kernel(const uint16_t* v, long long v_st, long long v_sh,
+                                                             const int* cu_k, int batch, int num_kv_heads,
+                                                             long long total_k, unsigned* emax) {
+  using S = VSlab<D>;
+  const int kvh = blockIdx.y;
+  const long long t0 = (long long)blockIdx.x * kVRows;
+  const int seq = slab_sequence(cu_k, batch, t0, total_k);
+  uint4 x[S::kPerThread];
+#pragma unroll
+  for (int i = 0; i < S::kPerThread; ++i) {
+    const int idx = threadIdx.x + i * kVThreads, r = idx / S::kVecs, c = idx % S::kVecs;
+    x[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (t0 + r < total_k) x[i] = __ldg(reinterpret_cast<const uint4*>(v + (t0 + r) * v_st + kvh * v_sh + c * 8));
+  }
+  unsigned mt = 0;
+#pragma unroll
+  for (int i = 0; i < S::kPerThread; ++i) {
+    const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+    unsigned m = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m = max(m, max(w[k] & 0x7fffu, (w[k] >> 16) & 0x7fffu));
+    if (seq >= 0) {
+      mt = max(mt, m);
+    } else {
+      const int r = (threadIdx.x + i * kVThreads) / S::kVecs;
+      if (t0 + r < total_k)
+        atomicMax(emax + (long long)seq_of_token(cu_k, batch, t0 + r) * num_kv_heads + kvh, m);
+    }
+  }
+  if (seq >= 0) {
+    __shared__ unsigned red[kVThreads / 32];
+    mt = __reduce_max_sync(0xffffffffu, mt);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned m = 0;
+#pragma unroll
+      for (int w = 0; w < kVThreads / 32; ++w) m = max(m, red[w]);
+      atomicMax(emax + (long long)seq * num_kv_heads + kvh, m);
+    }
+  }
+}
+
+// v16[t, kvh, :] = fp16(v[t, kvh, :] * 2^-e), e = pv_exponent(emax[b, kvh]): the
+// product is exact in fp32 (a power of two), below 2^15, and its fp16 rounding
+// is exact down to 2^-14 (smaller values, under 2^-28 of the row's largest,
+// keep an absolute error under 2^-25 of the scale).
+template <int D>
+__global__ void __launch_bounds__(kVThreads) v_to_half_kernel(const uint16_t* v, long long v_st, long long v_sh,
+                                                              const int* cu_k, int batch, int num_kv_heads,
+                                                              long long total_k, const unsigned* emax,
+                                                              uint16_t* v16) {
+  using S = VSlab<D>;
+  const int kvh = blockIdx.y;
+  const long long t0 = (long long)blockIdx.x * kVRows;
+  const int seq = slab_sequence(cu_k, batch, t0, total_k);
+  uint4 x[S::kPerThread];
+#pragma unroll
+  for (int i = 0; i < S::kPerThread; ++i) {
+    const int idx = threadIdx.x + i * kVThreads, r = idx / S::kVecs, c = idx % S::kVecs;
+    x[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (t0 + r < total_k) x[i] = __ldg(reinterpret_cast<const uint4*>(v + (t0 + r) * v_st + kvh * v_sh + c * 8));
+  }
+  const float f_slab = seq >= 0 ? __int_as_float((127 - pv_exponent(__ldg(emax + (long long)seq * num_kv_heads + kvh)))
+                                                 << 23)
+                                : 0.f;
+#pragma unroll
+  for (int i = 0; i < S::kPerThread; ++i) {
+    const int idx = threadIdx.x + i * kVThreads, r = idx / S::kVecs, c = idx % S::kVecs;
+    const long long t = t0 + r;
+    if (t >= total_k) continue;
+    float f = f_slab;  // 2^-e
+    if (seq < 0)
+      f = __int_as_float((127 - pv_exponent(__ldg(emax + (long long)seq_of_token(cu_k, batch, t) * num_kv_heads +
+                                                   kvh)))
+                         << 23);
+    const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      o[k] = pack2<__half>(__uint_as_float(w[k] << 16) * f, __uint_as_float(w[k] & 0xffff0000u) * f);
+    *reinterpret_cast<uint4*>(v16 + (t * num_kv_heads + kvh) * D + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace pre
 
 // =============================================================================
@@ -1035,21 +1191,82 @@ int* prefill_counters(int device, cudaStream_t stream) {
 using PrefillKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                                const pre::Params);
 
+// p_split 3 (fp16 P.V) reaches here only for bf16 inputs with packed K/V.
 template <typename T, int D, bool kPaged>
 PrefillKernel plan_prefill(const PrefillArgs& a, int p_split, pre::Params& p, dim3* grid) {
   using L = pre::Layout<D>;
+  constexpr bool kCanHalf = std::is_same<T, __nv_bfloat16>::value && !kPaged;
   const int pairs = (a.max_seqlen_q + L::kRowsPerCta - 1) / L::kRowsPerCta;
   p.batch = a.batch;
   p.num_pairs = pairs;
   const int device = current_device();
   const int g = sm_count(device);
-  p.sched = (p_split == 0 && prefill_schedule() == 0 && g > 0) ? prefill_counters(device, a.stream) : nullptr;
+  const bool rounded = p_split == 0 || p_split == 3;
+  p.sched = (rounded && prefill_schedule() == 0 && g > 0) ? prefill_counters(device, a.stream) : nullptr;
   if (p.sched != nullptr) {
     *grid = dim3(unsigned(g));
-    return pre::prefill_kernel<T, D, kPaged, false, true>;
+    if constexpr (kCanHalf) {
+      if (p_split == 3) return pre::prefill_kernel<T, D, kPaged, false, true, true>;
+    }
+    return pre::prefill_kernel<T, D, kPaged, false, true, false>;
   }
   *grid = dim3(unsigned(a.num_heads * a.batch), unsigned(pairs));
-  return p_split != 0 ? pre::prefill_kernel<T, D, kPaged, true, false> : pre::prefill_kernel<T, D, kPaged, false, false>;
+  if constexpr (kCanHalf) {
+    if (p_split == 3) return pre::prefill_kernel<T, D, kPaged, false, false, true>;
+  }
+  return rounded ? pre::prefill_kernel<T, D, kPaged, false, false, false>
+                 : pre::prefill_kernel<T, D, kPaged, true, false, false>;
+}
+
+// fp16 P.V scratch per (device, stream): the fp16 copy of V and the largest
+// |v| per (sequence, KV head).  Grown on demand (after the stream's earlier
+// work finished) and never freed; not grown while the stream is captured
+// (false: the caller feeds P as head + remainder instead).
+bool pv_scratch(int device, cudaStream_t stream, size_t v16_bytes, size_t emax_count, void** v16,
+                unsigned** emax) {
+  struct Buffers {
+    void* v16 = nullptr;
+    size_t v16_cap = 0;
+    unsigned* emax = nullptr;
+    size_t emax_cap = 0;
+  };
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, Buffers> scratch;
+  std::lock_guard<std::mutex> lock(mu);
+  Buffers& s = scratch[std::make_pair(device, reinterpret_cast<uintptr_t>(stream))];
+  if (s.v16_cap < v16_bytes || s.emax_cap < emax_count) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone ||
+        cudaStreamSynchronize(stream) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (s.v16_cap < v16_bytes) {
+      cudaFree(s.v16);
+      s.v16 = nullptr;
+      s.v16_cap = 0;
+      const size_t cap = v16_bytes + v16_bytes / 4;
+      if (cudaMalloc(&s.v16, cap) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+      }
+      s.v16_cap = cap;
+    }
+    if (s.emax_cap < emax_count) {
+      cudaFree(s.emax);
+      s.emax = nullptr;
+      s.emax_cap = 0;
+      const size_t cap = emax_count + emax_count / 4 + 64;
+      if (cudaMalloc(&s.emax, cap * sizeof(unsigned)) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+      }
+      s.emax_cap = cap;
+    }
+  }
+  *v16 = s.v16;
+  *emax = s.emax;
+  return true;
 }
 
 // Map of the 16-bit output {head_dim, head, token} in 64-column, 32-row boxes
@@ -1074,7 +1291,26 @@ int encode_out_map(const PrefillArgs& a, const CUtensorMap& placeholder, CUtenso
 template <typename T, int D>
 int launch_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
-  const int p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  int p_split = prefill_p_split(kBf16);
+  // fp16 P.V: V is read from an fp16 copy the pre-pass writes ([tokens, kv heads,
+  // dim], contiguous) into this stream's scratch.
+  PrefillArgs av = a;
+  unsigned* emax = nullptr;
+  if (p_split == 3) {
+    void* v16 = nullptr;
+    const size_t n_e = size_t(a.batch) * size_t(a.num_kv_heads);
+    const size_t bytes = size_t(a.total_k) * size_t(a.num_kv_heads) * size_t(D) * 2;
+    if (!kBf16) {
+      p_split = 0;  // fp16 inputs: P.V already runs in fp16
+    } else if (a.total_k > 0 && pv_scratch(current_device(), a.stream, bytes, n_e, &v16, &emax)) {
+      av.v = v16;
+      av.v_st = int64_t(a.num_kv_heads) * D;
+      av.v_sh = D;
+    } else {
+      p_split = 1;  // no scratch (stream being captured, or out of memory): head + remainder
+    }
+  }
   pre::Params p{};
   dim3 grid;
   const PrefillKernel kern = plan_prefill<T, D, false>(a, p_split, p, &grid);
@@ -1094,11 +1330,11 @@ int launch_t(const PrefillArgs& a) {
   {
     const uint64_t dims[3] = {uint64_t(D), uint64_t(a.num_kv_heads), uint64_t(a.total_k)};
     const uint64_t sk[2] = {uint64_t(a.k_sh) * 2, uint64_t(a.k_st) * 2};
-    const uint64_t sv[2] = {uint64_t(a.v_sh) * 2, uint64_t(a.v_st) * 2};
+    const uint64_t sv[2] = {uint64_t(av.v_sh) * 2, uint64_t(av.v_st) * 2};
     if (!encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.k, dims, sk, box, CU_TENSOR_MAP_SWIZZLE_128B,
                       &why))
       return invalid("prefill k: " + why);
-    if (!encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.v, dims, sv, box, CU_TENSOR_MAP_SWIZZLE_128B,
+    if (!encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, av.v, dims, sv, box, CU_TENSOR_MAP_SWIZZLE_128B,
                       &why))
       return invalid("prefill v: " + why);
   }
@@ -1118,6 +1354,22 @@ int launch_t(const PrefillArgs& a) {
   p.wait_ns = wait_limit_ns();
   p.expire = take_expire_request() ? 1 : 0;
   p.p_split = p_split;
+  p.num_kv_heads = a.num_kv_heads;
+  if (p_split == 3) {
+    // Pre-pass: largest |v| per (sequence, KV head), then the scaled fp16 copy.
+    p.pv_emax = emax;
+    e = cudaMemsetAsync(emax, 0, size_t(a.batch) * size_t(a.num_kv_heads) * sizeof(unsigned), a.stream);
+    if (e != cudaSuccess) return cuda_failure("prefill v pre-pass memset", e);
+    const dim3 vgrid(unsigned((a.total_k + pre::kVRows - 1) / pre::kVRows), unsigned(a.num_kv_heads));
+    const uint16_t* vsrc = static_cast<const uint16_t*>(a.v);
+    pre::v_absmax_kernel<D><<<vgrid, pre::kVThreads, 0, a.stream>>>(vsrc, a.v_st, a.v_sh, a.cu_k, a.batch,
+                                                                   a.num_kv_heads, a.total_k, emax);
+    pre::v_to_half_kernel<D><<<vgrid, pre::kVThreads, 0, a.stream>>>(
+        vsrc, a.v_st, a.v_sh, a.cu_k, a.batch, a.num_kv_heads, a.total_k, emax,
+        static_cast<uint16_t*>(const_cast<void*>(av.v)));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_failure("prefill v pre-pass launch", e);
+  }
   kern<<<grid, L::kThreads, L::kSmem, a.stream>>>(tq, tk, tv, to, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_failure("prefill launch", e);
@@ -1127,7 +1379,11 @@ int launch_t(const PrefillArgs& a) {
 template <typename T, int D>
 int launch_paged_t(const PrefillArgs& a) {
   using L = pre::Layout<D>;
-  const int p_split = prefill_p_split(std::is_same<T, __nv_bfloat16>::value);
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  int p_split = prefill_p_split(kBf16);
+  // fp16 P.V needs a copy of V, which a paged cache does not get: bf16 feeds P
+  // as head + remainder instead (fp16 inputs: P.V already runs in fp16).
+  if (p_split == 3) p_split = kBf16 ? 1 : 0;
   pre::Params p{};
   dim3 grid;
   const PrefillKernel kern = plan_prefill<T, D, true>(a, p_split, p, &grid);

@@ -29,14 +29,16 @@ HAS_CUDA_KERNELS = _lib.available()
 # remainder (a second P.V pass over that tile) whenever one of its keys holds
 # more than 1/16 of its row's probability sum so far ("adaptive"): every key
 # left rounded then weighs at most 1/16 in the output.
-P_SPLIT_MODES = {"auto": -1, "rounded": 0, "adaptive": 1, "all_tiles": 2}
+P_SPLIT_MODES = {"auto": -1, "rounded": 0, "adaptive": 1, "all_tiles": 2, "fp16_pv": 3}
 
 
 def set_p_precision(mode: str) -> str:
     """Set the P.V precision mode for later prefill launches; returns the previous one.
 
-    ``"auto"`` (default: bf16 ``"adaptive"``, fp16 ``"rounded"``), ``"rounded"``
-    (the reference's arithmetic), ``"adaptive"``, ``"all_tiles"``."""
+    ``"auto"`` (default: bf16 ``"fp16_pv"``, paged bf16 ``"adaptive"``, fp16
+    ``"rounded"``), ``"rounded"`` (the reference's arithmetic), ``"adaptive"``,
+    ``"all_tiles"``, ``"fp16_pv"`` (bf16, packed K/V: P.V in fp16 against a
+    scaled fp16 copy of V)."""
     if mode not in P_SPLIT_MODES:
         raise ValueError(f"unknown P precision mode {mode!r}; expected one of {sorted(P_SPLIT_MODES)}")
     prev = _lib.load().fat_set_prefill_p_split(P_SPLIT_MODES[mode])

@@ -88,7 +88,7 @@ void fat_expire_next_waits(int launches);
  * launches made after this call, from any thread.  The reference kernel
  * rounds P to the input dtype once (kernels/prefill.py:128); with bf16's 8-bit
  * significand that alone moves outputs of rows with few keys by up to ~4e-3.
- *   -1  automatic (default): bf16 uses mode 1, fp16 mode 0
+ *   -1  automatic (default): bf16 uses mode 3 (paged K/V: mode 1), fp16 mode 0
  *    0  P rounded to the input dtype once (the reference's arithmetic)
  *    1  a key tile's P enters as a 16-bit head plus a 16-bit remainder (a
  *       second P.V pass over that tile; ~2^-16 relative) when one of its keys
@@ -96,8 +96,16 @@ void fat_expire_next_waits(int launches);
  *       key ends with weight <= 1/16, so its rounding moves an output by at
  *       most 2^-12 of |v|
  *    2  head plus remainder on every key tile (twice the P.V work)
+ *    3  bf16 with packed K/V: P.V in fp16 -- P rounded to fp16 (~2^-12
+ *       relative), V read from an fp16 copy made by a pre-pass (two small
+ *       kernels on the call's stream) and scaled by 2^-e per (sequence, KV
+ *       head) so that any finite bf16 V fits, the output scaled back by 2^e.
+ *       The copy lives in a per-(device, stream) buffer of total_k * kv_heads *
+ *       head_dim * 2 bytes, grown on demand and never freed; a stream whose
+ *       buffer must grow while it is captured into a graph uses mode 1.  fp16
+ *       inputs treat it as mode 0, paged K/V as mode 1
  * Returns the previous setting, or -2 (message in fat_last_error) for a mode
- * outside [-1, 2].  No reference counterpart. */
+ * outside [-1, 3].  No reference counterpart. */
 int fat_set_prefill_p_split(int mode);
 
 /*

@@ -164,20 +164,44 @@ def test_prefill_head_dim_256_long_and_chunked():
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_p_precision_modes(dtype):
     """"all_tiles" keeps P to ~2^-16 everywhere; "rounded" is the reference
-    kernel's arithmetic (one rounding of P to the input dtype); "adaptive" (the
-    bf16 default) splits only tiles holding a key that weighs > 1/16 of its row."""
+    kernel's arithmetic (one rounding of P to the input dtype); "adaptive" splits
+    only tiles holding a key that weighs > 1/16 of its row; "fp16_pv" (the bf16
+    default) runs P.V in fp16 against a scaled fp16 copy of V (for fp16 inputs
+    it is "rounded")."""
     from flashattntile_b200.kernels.prefill import p_precision, set_p_precision
 
     q, k, v, cu_q, cu_k = varlen_case(13, [700, 130, 9], [700, 130, 9], 16, 4, 128, dtype)
     want = _oracle(q, k, v, cu_q, cu_k, True, dtype, out_f32=True)
-    errs = {}
-    for mode in ("rounded", "adaptive", "all_tiles"):
+    errs, outs = {}, {}
+    for mode in ("rounded", "adaptive", "all_tiles", "fp16_pv"):
         with p_precision(mode):
             out32 = _run(q, k, v, cu_q, cu_k, True, out_dtype=torch.float32)
+        outs[mode] = out32
         errs[mode] = float(np.abs(out32.cpu().numpy() - want).max())
     assert errs["all_tiles"] <= 1e-4, errs
     assert errs["adaptive"] <= 1e-3, errs
+    assert errs["fp16_pv"] <= 1e-3, errs
     assert errs["rounded"] <= (2e-3 if dtype == torch.float16 else 8e-3), errs
+    if dtype == torch.float16:
+        assert torch.equal(outs["fp16_pv"], outs["rounded"])
     assert set_p_precision("auto") == "auto"
     with pytest.raises(ValueError):
         set_p_precision("fp8")
+
+
+@pytest.mark.parametrize("vscale", [1e-3, 3e5, 1e12, 1e30])
+def test_fp16_pv_scales_any_bf16_range(vscale):
+    """bf16 V far outside fp16's range (and tiny V) through the fp16 P.V path: the
+    pre-pass scales each (sequence, KV head) by a power of two, so the result is
+    the oracle's to the same relative precision as at unit scale."""
+    from flashattntile_b200.kernels.prefill import p_precision
+
+    q, k, v, cu_q, cu_k = varlen_case(14, [300, 1, 777], [300, 1, 777], 8, 2, 128, torch.bfloat16)
+    v = (v.float() * vscale).to(torch.bfloat16)
+    v[300:301, 1] *= 0  # a sequence whose one token has an all-zero V row on one KV head
+    want = _oracle(q, k, v, cu_q, cu_k, True, torch.bfloat16, out_f32=True)
+    with p_precision("fp16_pv"):
+        out32 = _run(q, k, v, cu_q, cu_k, True, out_dtype=torch.float32)
+    got = out32.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - want).max() <= 1e-3 * vscale * 4

@@ -113,13 +113,17 @@ def test_paged_prefill_ignores_nan_past_sequence_ends(ps):
     assert_parity_16bit(out, want, torch.float16)
 
 
-def test_paged_equals_packed_prefill_bitwise():
-    """Same keys, read packed or through pages: identical outputs."""
-    from flashattntile_b200.kernels.prefill import launch_prefill
+@pytest.mark.parametrize("mode", ["adaptive", "rounded"])
+def test_paged_equals_packed_prefill_bitwise(mode):
+    """Same keys, read packed or through pages, same P precision mode: identical
+    outputs.  (bf16's default differs between the two: packed K/V runs P.V in
+    fp16 against a scaled fp16 copy of V, which a paged cache does not get.)"""
+    from flashattntile_b200.kernels.prefill import launch_prefill, p_precision
 
     kv_lens = [384, 1024, 256]
     q, k, v, table, lens, cu_q = _case(9, kv_lens, kv_lens, 8, 2, 128, 16, torch.bfloat16)
-    paged = _run(q, k, v, table, lens, cu_q, 16)
+    with p_precision(mode):
+        paged = _run(q, k, v, table, lens, cu_q, 16)
     ks, vs = [], []
     for b, n in enumerate(kv_lens):
         kb, vb = opaging.sequence_kv(to_np(k), to_np(v), to_np(table), n, b, 16)
@@ -129,9 +133,10 @@ def test_paged_equals_packed_prefill_bitwise():
 
     kp = from_np(np.concatenate(ks), torch.bfloat16).to(DEV)
     vp = from_np(np.concatenate(vs), torch.bfloat16).to(DEV)
-    packed = launch_prefill(q.to(DEV), kp, vp, cu_q.to(DEV), cu_q.to(DEV), max(kv_lens), max(kv_lens), True,
-                            128 ** -0.5)
-    torch.cuda.synchronize()
+    with p_precision(mode):
+        packed = launch_prefill(q.to(DEV), kp, vp, cu_q.to(DEV), cu_q.to(DEV), max(kv_lens), max(kv_lens), True,
+                                128 ** -0.5)
+        torch.cuda.synchronize()
     assert torch.equal(paged, packed)
 
 

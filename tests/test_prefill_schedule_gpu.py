@@ -78,7 +78,7 @@ def test_schedules_bitwise_equal(case, dtype, causal):
     assert torch.equal(a32, b32)
 
 
-@pytest.mark.parametrize("mode", ["rounded", "adaptive", "all_tiles"])
+@pytest.mark.parametrize("mode", ["rounded", "adaptive", "all_tiles", "fp16_pv"])
 def test_schedules_bitwise_equal_for_every_p_precision(mode):
     from flashattntile_b200.kernels.prefill import p_precision
 
