@@ -1063,14 +1063,14 @@ __global__ void __launch_bounds__(kVThreads) v_absmax_kernel(const uint16_t* v, 
   using S = VSlab<D>;
   const int kvh = blockIdx.y;
   const long long t0 = (long long)blockIdx.x * kVRows;
-  const int seq = slab_sequence(cu_k, batch, t0, total_k);
-  uint4 x[S::kPerThread];
+  uint4 x[S::kPerThread];  // loads first: the sequence lookup overlaps their latency
 #pragma unroll
   for (int i = 0; i < S::kPerThread; ++i) {
     const int idx = threadIdx.x + i * kVThreads, r = idx / S::kVecs, c = idx % S::kVecs;
     x[i] = make_uint4(0u, 0u, 0u, 0u);
     if (t0 + r < total_k) x[i] = __ldg(reinterpret_cast<const uint4*>(v + (t0 + r) * v_st + kvh * v_sh + c * 8));
   }
+  const int seq = slab_sequence(cu_k, batch, t0, total_k);
   unsigned mt = 0;
 #pragma unroll
   for (int i = 0; i < S::kPerThread; ++i) {
@@ -1112,14 +1112,14 @@ __global__ void __launch_bounds__(kVThreads) v_to_half_kernel(const uint16_t* v,
   using S = VSlab<D>;
   const int kvh = blockIdx.y;
   const long long t0 = (long long)blockIdx.x * kVRows;
-  const int seq = slab_sequence(cu_k, batch, t0, total_k);
-  uint4 x[S::kPerThread];
+  uint4 x[S::kPerThread];  // loads first: the sequence lookup overlaps their latency
 #pragma unroll
   for (int i = 0; i < S::kPerThread; ++i) {
     const int idx = threadIdx.x + i * kVThreads, r = idx / S::kVecs, c = idx % S::kVecs;
     x[i] = make_uint4(0u, 0u, 0u, 0u);
     if (t0 + r < total_k) x[i] = __ldg(reinterpret_cast<const uint4*>(v + (t0 + r) * v_st + kvh * v_sh + c * 8));
   }
+  const int seq = slab_sequence(cu_k, batch, t0, total_k);
   const float f_slab = seq >= 0 ? __int_as_float((127 - pv_exponent(__ldg(emax + (long long)seq * num_kv_heads + kvh)))
                                                  << 23)
                                 : 0.f;
