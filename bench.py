@@ -536,47 +536,48 @@ def run_comparators(device, args, peaks) -> dict:
     offs = [0] + torch.tensor(CFG3_LENS).cumsum(0).tolist()
     cu = torch.tensor(offs, dtype=torch.int32, device=device)
     g3 = torch.Generator(device=device).manual_seed(2)
-    sets = []
-    for _ in range(2):
-        sets.append(tuple(torch.randn((offs[-1], h, 128), generator=g3, device=device).half() for h in (32, 8, 8)))
-    ref3 = launch_prefill(*sets[1], cu, cu, 4096, 4096, True, 128 ** -0.5)
+    for dt, tag in ((torch.float16, ""), (torch.bfloat16, "_bf16")):
+        sets = []
+        for _ in range(2):
+            sets.append(tuple(torch.randn((offs[-1], h, 128), generator=g3, device=device).to(dt) for h in (32, 8, 8)))
+        ref3 = launch_prefill(*sets[1], cu, cu, 4096, 4096, True, 128 ** -0.5)
 
-    def alternate(call):
-        state = {"i": 0}  # the first call uses sets[1], the set ref3 was computed on
+        def alternate(call):
+            state = {"i": 0}  # the first call uses sets[1], the set ref3 was computed on
 
-        def fn():
-            state["i"] += 1
-            return call(*sets[state["i"] & 1])
-        return fn
+            def fn():
+                state["i"] += 1
+                return call(*sets[state["i"] & 1])
+            return fn
 
-    o3 = torch.empty_like(sets[0][0])
-    record("cfg3_prefill_ours", alternate(lambda q3, k3, v3: launch_prefill(q3, k3, v3, cu, cu, 4096, 4096, True,
-                                                                            128 ** -0.5, out=o3)),
-           ref3, flops, "TFLOP/s")
-
-    def sdpa(q3, k3, v3):
-        import torch.nn.functional as F
-
-        outs = []
-        for a, b in zip(offs[:-1], offs[1:]):
-            o = F.scaled_dot_product_attention(q3[a:b].transpose(0, 1)[None], k3[a:b].transpose(0, 1)[None],
-                                               v3[a:b].transpose(0, 1)[None], is_causal=True, scale=128 ** -0.5,
-                                               enable_gqa=True)
-            outs.append(o[0].transpose(0, 1))
-        return torch.cat(outs)
-
-    record("cfg3_prefill_torch_sdpa", alternate(sdpa), ref3, flops, "TFLOP/s")
-    try:
-        from flash_attn import flash_attn_varlen_func
-
-        record("cfg3_prefill_flash_attn2",
-               alternate(lambda q3, k3, v3: flash_attn_varlen_func(q3, k3, v3, cu, cu, 4096, 4096,
-                                                                   softmax_scale=128 ** -0.5, causal=True)),
+        o3 = torch.empty_like(sets[0][0])
+        record("cfg3_prefill_ours" + tag,
+               alternate(lambda q3, k3, v3: launch_prefill(q3, k3, v3, cu, cu, 4096, 4096, True, 128 ** -0.5, out=o3)),
                ref3, flops, "TFLOP/s")
-    except Exception as e:
-        res["cfg3_prefill_flash_attn2"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
-    del sets, ref3, o3
-    torch.cuda.empty_cache()
+
+        def sdpa(q3, k3, v3):
+            import torch.nn.functional as F
+
+            outs = []
+            for a, b in zip(offs[:-1], offs[1:]):
+                o = F.scaled_dot_product_attention(q3[a:b].transpose(0, 1)[None], k3[a:b].transpose(0, 1)[None],
+                                                   v3[a:b].transpose(0, 1)[None], is_causal=True, scale=128 ** -0.5,
+                                                   enable_gqa=True)
+                outs.append(o[0].transpose(0, 1))
+            return torch.cat(outs)
+
+        record("cfg3_prefill_torch_sdpa" + tag, alternate(sdpa), ref3, flops, "TFLOP/s")
+        try:
+            from flash_attn import flash_attn_varlen_func
+
+            record("cfg3_prefill_flash_attn2" + tag,
+                   alternate(lambda q3, k3, v3: flash_attn_varlen_func(q3, k3, v3, cu, cu, 4096, 4096,
+                                                                       softmax_scale=128 ** -0.5, causal=True)),
+                   ref3, flops, "TFLOP/s")
+        except Exception as e:
+            res["cfg3_prefill_flash_attn2" + tag] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+        del sets, ref3, o3
+        torch.cuda.empty_cache()
     # The reference's Triton kernels (cfg2 decode at split_k 1/2/4/8, cfg3 prefill), in a process of their own.
     import subprocess
 
