@@ -205,3 +205,26 @@ def test_fp16_pv_scales_any_bf16_range(vscale):
     got = out32.cpu().numpy()
     assert np.isfinite(got).all()
     assert np.abs(got - want).max() <= 1e-3 * vscale * 4
+
+
+def test_fp16_pv_rejects_misaligned_v_through_the_c_abi():
+    """A C caller's bf16 V that is not 16-byte aligned is refused before anything runs: the fp16 P.V
+    pre-pass reads V in 16-byte vectors, and its tensor map describes the fp16 copy, not V, so the
+    entry point's own alignment check is what guards it."""
+    from flashattntile_b200 import _lib
+
+    lib = _lib.load()
+    q, k, v, cu_q, cu_k = (t.to(DEV) for t in varlen_case(15, [64, 40], [64, 40], 4, 2, 128, torch.bfloat16))
+    vbuf = torch.zeros(v.numel() + 8, dtype=torch.bfloat16, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.fat_prefill_varlen(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), vbuf.data_ptr() + 2,
+        v.stride(0), v.stride(1), out.data_ptr(), out.stride(0), out.stride(1), cu_q.data_ptr(), cu_k.data_ptr(), 2,
+        q.shape[0], k.shape[0], 4, 2, 128, 64, 64, 1, 128 ** -0.5, _lib.DTYPE_CODE[torch.bfloat16],
+        _lib.DTYPE_CODE[torch.bfloat16], err.data_ptr(), stream)
+    assert rc == _lib.FAT_ERR_UNSUPPORTED
+    assert b"16-byte" in lib.fat_last_error()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
