@@ -160,6 +160,13 @@ def launch_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen
     q, k, v = aligned(q), aligned(k), aligned(v)
     cu_seqlens_q = cu_seqlens_q.contiguous()
     cu_seqlens_k = cu_seqlens_k.contiguous()
+    if out is not None:
+        # A given output fixes the dtype the kernel writes.
+        if out_dtype is not None and out_dtype != out.dtype:
+            raise ValueError(f"out_dtype {out_dtype} does not match out's dtype {out.dtype}")
+        if out.shape != q.shape or not out.is_cuda:
+            raise ValueError(f"out must be a CUDA tensor of q's shape {tuple(q.shape)}, got {tuple(out.shape)}")
+        out_dtype = out.dtype
     out_dtype = out_dtype or q.dtype
     if out is None:
         out = torch.empty(q.shape, dtype=out_dtype, device=dev)
