@@ -166,6 +166,13 @@ def prepare_decode(q, k_cache, v_cache, page_table, seq_lens, page_size, softmax
         seq_lens = seq_lens.contiguous()
     batch, heads, dim = q.shape
     kvh = k_cache.shape[2]
+    if out is not None:
+        # A given output fixes the dtype the kernel writes.
+        if out_dtype is not None and out_dtype != out.dtype:
+            raise ValueError(f"out_dtype {out_dtype} does not match out's dtype {out.dtype}")
+        if tuple(out.shape) != (batch, heads, dim) or not out.is_cuda:
+            raise ValueError(f"out must be a CUDA tensor of shape {(batch, heads, dim)}, got {tuple(out.shape)}")
+        out_dtype = out.dtype
     out_dtype = out_dtype or q.dtype
     own_out = out is None
     if out is None:
