@@ -63,6 +63,8 @@ def test_host_side_validation_errors_without_gpu():
     rc = lib.fat_prefill_varlen(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, None, None, 1, 1, 1, 4, 2, 64, 1, 1,
                                 1, 0.1, 2, 2, None, None)
     assert rc == _lib.FAT_ERR_UNSUPPORTED and b"fp16 or bf16" in lib.fat_last_error()
+    # process-wide switches: values outside their range are refused
+    assert lib.fat_set_prefill_schedule(2) == -2 and b"schedule" in lib.fat_last_error()
 
 
 def test_status_codes_map_to_python_exceptions():
