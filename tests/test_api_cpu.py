@@ -162,6 +162,41 @@ def test_decode_validation_errors():
         paged_decode_attention(torch.randn(2, 4, 16, dtype=torch.float16), cache, config={"split_k": 0})
 
 
+
+DECODE_BAD_CONFIGS = [
+    # (config, message of decode.py:474-500)
+    ({"bogus": 1}, "unknown decode config keys: ['bogus']"),
+    ({"split_k": 0}, "split_k must be a positive integer, got 0"),
+    ({"split_k": 2.0}, "split_k must be a positive integer, got 2.0"),
+    ({"split_k": 65}, "split_k must be <= 64, got 65"),
+    ({"num_warps": 3}, "num_warps must be a power of two <= 32, got 3"),
+    ({"num_warps": 64}, "num_warps must be a power of two <= 32, got 64"),
+    ({"num_stages": 0}, "num_stages must be >= 1, got 0"),
+]
+
+
+@pytest.mark.parametrize("config,message", DECODE_BAD_CONFIGS)
+def test_decode_config_is_refused_with_the_reference_messages(config, message):
+    with pytest.raises(ValueError) as exc:
+        paged_decode_attention(torch.randn(2, 4, 16, dtype=torch.float16), _cpu_cache(), config=config)
+    assert message in str(exc.value)
+
+
+def test_decode_inputs_are_refused_with_the_reference_messages():
+    """decode.py:503-522: exception type and message per malformed input (checks that need no GPU)."""
+    cache = _cpu_cache()
+    with pytest.raises(TypeError, match="cache must be a PagedKVCache"):
+        paged_decode_attention(torch.randn(2, 4, 16, dtype=torch.float16), object())
+    with pytest.raises(ValueError, match=r"q must be \[batch, heads, head_dim\], got \(2, 64\)"):
+        paged_decode_attention(torch.randn(2, 64, dtype=torch.float16), cache)
+    with pytest.raises(ValueError, match="q must be floating point, got torch.int16"):
+        paged_decode_attention(torch.zeros(2, 4, 16, dtype=torch.int16), cache)
+    with pytest.raises(ValueError, match="q head_dim 8 != cache head_dim 16"):
+        paged_decode_attention(torch.randn(2, 4, 8, dtype=torch.float16), cache)
+    with pytest.raises(ValueError, match="num_heads 3 must be divisible by num_kv_heads 2"):
+        paged_decode_attention(torch.randn(2, 3, 16, dtype=torch.float16), cache)
+
+
 def test_zero_length_sequence_is_rejected_for_decode():
     cache = _cpu_cache(lens=(4, 4))
     cache.seq_lens[1] = 0
@@ -179,6 +214,60 @@ def test_prefill_config_and_offsets_are_validated():
     bad = torch.tensor([0, 5], dtype=torch.int32)
     with pytest.raises(ValueError, match="must equal q.shape"):
         prefill_attention(torch.randn(4, 2, 16, dtype=torch.float16), q, q, bad, bad, 4, 4)
+
+
+
+def _prefill_case(**over):
+    """Valid CPU inputs for prefill_attention (2 sequences of 3 and 2 tokens, 4 / 2 heads), with overrides."""
+    f16 = torch.float16
+    args = dict(q=torch.randn(5, 4, 16, dtype=f16), k=torch.randn(6, 2, 16, dtype=f16),
+                v=torch.randn(6, 2, 16, dtype=f16), cu_q=torch.tensor([0, 3, 5], dtype=torch.int32),
+                cu_k=torch.tensor([0, 3, 6], dtype=torch.int32), causal=True)
+    args.update(over)
+    return args
+
+
+PREFILL_BAD_INPUTS = [
+    # (overrides, message of prefill.py:194-233, in the order the checks run)
+    (dict(q=torch.randn(5, 64, dtype=torch.float16)), "must be 3-D"),
+    (dict(v=torch.randn(6, 2, 8, dtype=torch.float16)), "k shape (6, 2, 16) != v shape (6, 2, 8)"),
+    (dict(q=torch.randn(5, 4, 8, dtype=torch.float16)), "q head_dim 8 != k head_dim 16"),
+    (dict(q=torch.randn(5, 4, 16, dtype=torch.bfloat16)), "dtype mismatch"),
+    (dict(q=torch.zeros(5, 4, 16, dtype=torch.int16), k=torch.zeros(6, 2, 16, dtype=torch.int16),
+          v=torch.zeros(6, 2, 16, dtype=torch.int16)), "expected floating point inputs"),
+    (dict(cu_q=torch.tensor([[0, 3, 5]], dtype=torch.int32)), "must be 1-D"),
+    (dict(cu_k=torch.tensor([0, 6], dtype=torch.int32)), "same batch dimension"),
+    (dict(cu_q=torch.tensor([5], dtype=torch.int32), cu_k=torch.tensor([6], dtype=torch.int32)),
+     "at least batch + 1 entries"),
+    (dict(cu_q=torch.tensor([0, 3, 5], dtype=torch.int64)), "must be int32"),
+    (dict(cu_q=torch.tensor([1, 3, 5], dtype=torch.int32)), "must start at 0"),
+    (dict(cu_q=torch.tensor([0, 3, 4], dtype=torch.int32)), "cu_seqlens_q[-1] must equal q.shape[0]"),
+    (dict(cu_k=torch.tensor([0, 3, 7], dtype=torch.int32)), "cu_seqlens_k[-1] must equal k.shape[0]"),
+    (dict(cu_q=torch.tensor([0, 0, 3, 2, 5], dtype=torch.int32), cu_k=torch.tensor([0, 1, 3, 4, 6], dtype=torch.int32)),
+     "cu_seqlens_q must be non-decreasing"),
+    (dict(cu_q=torch.tensor([0, 1, 3, 4, 5], dtype=torch.int32), cu_k=torch.tensor([0, 3, 2, 4, 6], dtype=torch.int32)),
+     "cu_seqlens_k must be non-decreasing"),
+    (dict(cu_k=torch.tensor([0, 2, 6], dtype=torch.int32)), "requires kv_len >= q_len per sequence"),
+    (dict(k=torch.randn(6, 3, 16, dtype=torch.float16), v=torch.randn(6, 3, 16, dtype=torch.float16)),
+     "num_heads (4) must be divisible by num_kv_heads (3)"),
+]
+
+
+@pytest.mark.parametrize("over,message", PREFILL_BAD_INPUTS)
+def test_prefill_inputs_are_refused_with_the_reference_messages(over, message):
+    """Every check of prefill.py:194-233 that needs no GPU, hit by its own input, with its message."""
+    a = _prefill_case(**over)
+    with pytest.raises(ValueError) as exc:
+        prefill_attention(a["q"], a["k"], a["v"], a["cu_q"], a["cu_k"], 3, 3, causal=a["causal"])
+    assert message in str(exc.value)
+
+
+def test_prefill_kv_shorter_than_q_is_allowed_without_the_causal_mask():
+    """The kv_len >= q_len rule is the causal alignment's; the checks pass without it (the launch then
+    refuses CPU tensors: there is no CPU path)."""
+    a = _prefill_case(cu_k=torch.tensor([0, 2, 6], dtype=torch.int32), causal=False)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        prefill_attention(a["q"], a["k"], a["v"], a["cu_q"], a["cu_k"], 3, 4, causal=False)
 
 
 # --------------------------------------------------------------------------- work accounting
