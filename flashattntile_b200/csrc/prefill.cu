@@ -80,7 +80,7 @@ struct Params {
   int p_split;           // P into P.V as head + remainder: 0 never, 1 where a key weighs (vote), 2 always
   int batch, num_pairs;  // sequences; 2-tile query pairs of the longest sequence
   int* sched;            // kPersist: {next rank, CTAs done}, zero at launch and zeroed again by the last CTA
-  const unsigned* pv_emax;  // kHalfPV: largest |v| (bf16 bits) per (sequence, KV head), b * Hkv + kv head
+  const unsigned* pv_emax;  // kHalfPV: largest finite |v| (bf16 bits) per (sequence, KV head), b * Hkv + kv head
   int num_kv_heads;
 };
 
@@ -160,8 +160,8 @@ struct Work {
 };
 
 // kHalfPV: V of (sequence, KV head) was stored as fp16 times 2^-e, e = E - 14
-// for E the binary exponent of its largest |v|: every scaled value is below
-// 2^15 (inside fp16's range) and the largest at least 2^14 (small V keeps
+// for E the binary exponent of its largest finite |v|: every finite scaled
+// value is below 2^15 (inside fp16's range) and the largest at least 2^14 (small V keeps
 // fp16's full precision); the output is scaled back by 2^e.  e is kept in
 // [-100, 114] so that 2^e and 2^-e are normal floats (an all-zero V gets -100).
 __host__ __device__ __forceinline__ int pv_exponent(unsigned absmax_bits) {
@@ -1033,6 +1033,9 @@ __device__ __forceinline__ int seq_of_token(const int* cu, int batch, long long 
   return lo;
 }
 
+// A bf16 magnitude (sign cleared), or 0 for inf and NaN (exponent bits all ones).
+__device__ __forceinline__ unsigned finite_mag(unsigned mag) { return mag < 0x7f80u ? mag : 0u; }
+
 template <int D>
 struct VSlab {
   static constexpr int kVecs = D / 8;                          // 16-byte vectors per token row
@@ -1052,10 +1055,11 @@ __device__ __forceinline__ int slab_sequence(const int* cu_k, int batch, long lo
   return seq;
 }
 
-// Largest |v| per (sequence, KV head) as bf16 bits without the sign (a bf16
-// magnitude orders like its bit pattern; NaN compares above inf), into emax
-// (zeroed before): one atomic per slab (per token in a slab that straddles
-// sequences).
+// Largest finite |v| per (sequence, KV head) as bf16 bits without the sign (a
+// bf16 magnitude orders like its bit pattern), into emax (zeroed before): one
+// atomic per slab (per token in a slab that straddles sequences).  inf and NaN
+// are left out: they convert to fp16 inf and NaN whatever the scale, and a
+// scale set by them would flush every finite value of the sequence to zero.
 template <int D>
 __global__ void __launch_bounds__(kVThreads) v_absmax_kernel(const uint16_t* v, long long v_st, long long v_sh,
                                                              const int* cu_k, int batch, int num_kv_heads,
@@ -1077,7 +1081,7 @@ __global__ void __launch_bounds__(kVThreads) v_absmax_kernel(const uint16_t* v, 
     const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
     unsigned m = 0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) m = max(m, max(w[k] & 0x7fffu, (w[k] >> 16) & 0x7fffu));
+    for (int k = 0; k < 4; ++k) m = max(m, max(finite_mag(w[k] & 0x7fffu), finite_mag((w[k] >> 16) & 0x7fffu)));
     if (seq >= 0) {
       mt = max(mt, m);
     } else {
@@ -1356,7 +1360,7 @@ int launch_t(const PrefillArgs& a) {
   p.p_split = p_split;
   p.num_kv_heads = a.num_kv_heads;
   if (p_split == 3) {
-    // Pre-pass: largest |v| per (sequence, KV head), then the scaled fp16 copy.
+    // Pre-pass: largest finite |v| per (sequence, KV head), then the scaled fp16 copy.
     p.pv_emax = emax;
     e = cudaMemsetAsync(emax, 0, size_t(a.batch) * size_t(a.num_kv_heads) * sizeof(unsigned), a.stream);
     if (e != cudaSuccess) return cuda_failure("prefill v pre-pass memset", e);

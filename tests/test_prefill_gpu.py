@@ -207,6 +207,31 @@ def test_fp16_pv_scales_any_bf16_range(vscale):
     assert np.abs(got - want).max() <= 1e-3 * vscale * 4
 
 
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_fp16_pv_keeps_finite_columns_when_v_holds_inf_or_nan(causal):
+    """An inf or NaN in bf16 V leaves the other columns of its (sequence, KV head) intact on the fp16
+    P.V path, as on the paths that read V directly: the pre-pass's scale comes from the largest finite
+    |v| (inf and NaN convert as they are), so no finite value is flushed by a scale set for an inf.
+    The non-finite outputs sit where the direct path has them; every finite one matches it."""
+    from flashattntile_b200.kernels.prefill import p_precision
+
+    q, k, v, cu_q, cu_k = varlen_case(16, [300, 257, 40], [300, 257, 40], 8, 2, 128, torch.bfloat16)
+    v[150, 0, 5] = float("inf")   # sequence 0, KV head 0, column 5
+    v[400, 1, 7] = float("nan")   # sequence 1, KV head 1, column 7
+    outs = {}
+    for mode in ("fp16_pv", "all_tiles"):
+        with p_precision(mode):
+            outs[mode] = _run(q, k, v, cu_q, cu_k, causal, out_dtype=torch.float32).cpu()
+    a, b = outs["fp16_pv"], outs["all_tiles"]
+    fin = torch.isfinite(b)
+    assert torch.equal(torch.isfinite(a), fin)
+    assert not fin.all()
+    assert (a[fin] - b[fin]).abs().max().item() <= 2e-3
+    # Columns other than the poisoned ones stay finite everywhere.
+    assert torch.isfinite(a[:, :, [c for c in range(128) if c not in (5, 7)]]).all()
+
+
 def test_fp16_pv_rejects_misaligned_v_through_the_c_abi():
     """A C caller's bf16 V that is not 16-byte aligned is refused before anything runs: the fp16 P.V
     pre-pass reads V in 16-byte vectors, and its tensor map describes the fp16 copy, not V, so the
